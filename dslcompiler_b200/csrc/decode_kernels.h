@@ -1,0 +1,27 @@
+// decode_kernels.h -- launch interface of the small-M (decode) SwiGLU kernel.
+#pragma once
+
+#include <cuda.h>
+#include <cuda_runtime.h>
+
+#include <cstddef>
+#include <cstdint>
+
+namespace llk_b200 {
+
+struct DecodePlan {
+  int block_m, block_n, block_k, stages, split_k, grid, threads, smem_bytes;
+};
+
+// Largest M the decode kernel serves.
+int decode_max_m();
+// Whether the decode kernel handles this shape / output type.
+bool decode_supported(int64_t M, int64_t N, int64_t K, int y_f32);
+DecodePlan decode_plan(int64_t M, int64_t N, int64_t K, int sm_count);
+// Device workspace the launch needs (split-K partial sums + tile counters).
+size_t decode_workspace_bytes(int64_t M, int64_t N, int64_t K, int sm_count);
+cudaError_t decode_launch(const CUtensorMap &wg, const CUtensorMap &wu, const void *x, int64_t ldx, void *y,
+                          int64_t ldy, int y_f32, int64_t M, int64_t N, int64_t K, void *workspace, int *status,
+                          int sm_count, cudaStream_t stream);
+
+}  // namespace llk_b200

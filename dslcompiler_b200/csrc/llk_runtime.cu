@@ -1,0 +1,715 @@
+// llk_runtime.cu -- host side of the C ABI declared in include/llk_b200.h:
+// argument checks (the llk.fused_swiglu verifier rules), kernel selection,
+// TMA descriptor encoding, host<->device staging for host buffers, the
+// packed-weight store, the launch-plan cache and the device probe.
+//
+// Host code only; the kernels live in swiglu_tc.cu, swiglu_decode.cu and
+// swiglu_simt.cu.  No CPU compute path exists: every result is produced by a
+// CUDA kernel.
+#include <cuda.h>
+#include <cuda_runtime.h>
+#include <cudaTypedefs.h>
+
+#include <cstdint>
+#include <cstdlib>
+#include <cstring>
+#include <list>
+#include <mutex>
+#include <string>
+#include <unordered_map>
+#include <vector>
+
+#include "decode_kernels.h"
+#include "llk_b200.h"
+#include "tc_kernels.h"
+
+using namespace llk_b200;
+
+namespace {
+
+constexpr uint64_t kLibraryVersion = 0x00010000ull;  // 0.1.0
+constexpr int kMaxDevices = 64;
+
+thread_local int g_last_status = LLK_OK;
+
+// ------------------------------------------------------------ device state
+struct DeviceBuffer {
+  void *ptr = nullptr;
+  size_t bytes = 0;
+  cudaError_t ensure(size_t need) {
+    if (need <= bytes) return cudaSuccess;
+    if (ptr) cudaFree(ptr);
+    ptr = nullptr;
+    bytes = 0;
+    size_t alloc = need + need / 8;
+    cudaError_t e = cudaMalloc(&ptr, alloc);
+    if (e == cudaSuccess) bytes = alloc;
+    return e;
+  }
+};
+
+struct DeviceState {
+  bool ready = false;
+  int sm_count = 0;
+  int cc_major = 0, cc_minor = 0;
+  int *status = nullptr;       // device error word written by the kernels
+  DeviceBuffer stage[4];       // host-staging buffers: x, wg, wu, y
+  DeviceBuffer workspace;      // split-K partials when the caller gives no scratch
+  std::mutex mu;
+};
+
+DeviceState g_dev[kMaxDevices];
+std::mutex g_init_mu;
+
+PFN_cuTensorMapEncodeTiled_v12000 g_encode = nullptr;
+
+int resolve_device(const llk_gpu_context *gpu, int *dev_out) {
+  int dev = gpu ? gpu->device : -1;
+  if (dev < 0) {
+    if (cudaGetDevice(&dev) != cudaSuccess) return LLK_ERR_DEVICE;
+  }
+  if (dev >= kMaxDevices) return LLK_ERR_ARG;
+  *dev_out = dev;
+  return LLK_OK;
+}
+
+// Makes `dev` current and initialises its state once.
+int device_init(int dev, DeviceState **out) {
+  int count = 0;
+  if (cudaGetDeviceCount(&count) != cudaSuccess || count <= 0) {
+    cudaGetLastError();
+    return LLK_ERR_DEVICE;
+  }
+  if (dev >= count) return LLK_ERR_ARG;
+  if (cudaSetDevice(dev) != cudaSuccess) return LLK_ERR_DEVICE;
+  DeviceState &s = g_dev[dev];
+  std::lock_guard<std::mutex> lk(g_init_mu);
+  if (!s.ready) {
+    cudaDeviceProp prop;
+    if (cudaGetDeviceProperties(&prop, dev) != cudaSuccess) return LLK_ERR_DEVICE;
+    s.cc_major = prop.major;
+    s.cc_minor = prop.minor;
+    s.sm_count = prop.multiProcessorCount;
+    if (prop.major != 10 || prop.minor != 0) return LLK_ERR_DEVICE;  // sm_100 only
+    if (cudaMalloc(&s.status, sizeof(int)) != cudaSuccess) return LLK_ERR_CUDA;
+    if (cudaMemset(s.status, 0, sizeof(int)) != cudaSuccess) return LLK_ERR_CUDA;
+    if (!g_encode) {
+      void *fn = nullptr;
+      cudaDriverEntryPointQueryResult q;
+      if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &fn, cudaEnableDefault, &q) != cudaSuccess ||
+          q != cudaDriverEntryPointSuccess || fn == nullptr)
+        return LLK_ERR_DEVICE;
+      g_encode = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(fn);
+    }
+    s.ready = true;
+  }
+  *out = &s;
+  return LLK_OK;
+}
+
+bool is_device_ptr(const void *p) {
+  if (!p) return false;
+  cudaPointerAttributes a;
+  if (cudaPointerGetAttributes(&a, p) != cudaSuccess) {
+    cudaGetLastError();
+    return false;
+  }
+  return a.type == cudaMemoryTypeDevice || a.type == cudaMemoryTypeManaged;
+}
+
+// 2-D bf16 tensor map: dims {inner, outer}, row pitch in bytes, box
+// {box_inner, box_outer}, 128-byte swizzle, zero fill out of bounds.
+int encode_tmap(CUtensorMap *m, const void *base, uint64_t inner, uint64_t outer, uint64_t pitch_bytes,
+                uint32_t box_inner, uint32_t box_outer) {
+  cuuint64_t dims[2] = {inner, outer};
+  cuuint64_t strides[1] = {pitch_bytes};
+  cuuint32_t box[2] = {box_inner, box_outer};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = g_encode(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void *>(base), dims, strides, box, estr,
+                        CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                        CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS ? LLK_OK : LLK_ERR_ALIGN;
+}
+
+bool aligned16(const void *p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+// ------------------------------------------------------------- plan cache
+struct PlanCache {
+  struct Entry {
+    std::string key;
+    llk_launch_plan plan;
+  };
+  std::list<Entry> lru;
+  std::unordered_map<std::string, std::list<Entry>::iterator> index;
+  size_t max_entries = 1024;
+  uint64_t hits = 0, misses = 0, evictions = 0;
+  std::mutex mu;
+};
+PlanCache g_cache;
+
+std::string key_bytes(const llk_kernel_key &k) {
+  return std::string(reinterpret_cast<const char *>(&k), sizeof(k));
+}
+
+llk_kernel_key make_key(int op, int out_dtype, int64_t M, int64_t N, int64_t K, int variant) {
+  llk_kernel_key k;
+  std::memset(&k, 0, sizeof(k));
+  k.operation = static_cast<uint8_t>(op);
+  k.input_type = LLK_DTYPE_BF16;
+  k.output_type = static_cast<uint8_t>(out_dtype);
+  k.M_bucket = llk_classify_m(M);
+  k.N = N;
+  k.K = K;
+  k.weight_layout = 0;
+  k.isa = LLK_ISA_SM100A;
+  k.math_mode = 0;  // strict exp, the fused path's epilogue
+  k.thread_count = static_cast<uint16_t>(variant);
+  k.compiler_version = kLibraryVersion;
+  k.schedule_version = 1;
+  return k;
+}
+
+// Kernel family for a request: the decode kernel for small M when its
+// shape rules hold, the tcgen05 kernel otherwise; SIMT when TMA cannot
+// describe the operands.
+int choose_variant(int requested, bool tma_ok, bool decode_ok, int64_t M, int64_t K) {
+  if (requested == LLK_VARIANT_SIMT) return LLK_VARIANT_SIMT;
+  if (!tma_ok || K == 0) return requested == LLK_VARIANT_AUTO ? LLK_VARIANT_SIMT : -1;
+  if (requested == LLK_VARIANT_TC) return LLK_VARIANT_TC;
+  if (requested == LLK_VARIANT_DECODE) return decode_ok ? LLK_VARIANT_DECODE : -1;
+  if (decode_ok && M <= decode_max_m()) return LLK_VARIANT_DECODE;
+  return LLK_VARIANT_TC;
+}
+
+llk_launch_plan build_plan(int variant, int op, int64_t M, int64_t N, int64_t K, int sm_count) {
+  llk_launch_plan p;
+  std::memset(&p, 0, sizeof(p));
+  p.variant = variant;
+  if (variant == LLK_VARIANT_TC) {
+    const int mode = (op == LLK_OP_MATMUL) ? TC_MATMUL_F32 : TC_SWIGLU_BF16;
+    p.block_m = 128;
+    p.block_n = tc_tile_n(mode);
+    p.block_k = 64;
+    p.stages = 4;
+    p.split_k = 1;
+    const int64_t tiles = ((M + 127) / 128) * ((N + p.block_n - 1) / p.block_n);
+    p.grid = static_cast<int>(tiles < sm_count ? tiles : sm_count);
+    p.threads = tc_threads();
+    p.smem_bytes = tc_smem_bytes();
+  } else if (variant == LLK_VARIANT_DECODE) {
+    DecodePlan d = decode_plan(M, N, K, sm_count);
+    p.block_m = d.block_m;
+    p.block_n = d.block_n;
+    p.block_k = d.block_k;
+    p.stages = d.stages;
+    p.split_k = d.split_k;
+    p.grid = d.grid;
+    p.threads = d.threads;
+    p.smem_bytes = d.smem_bytes;
+  } else {
+    p.block_m = 1;
+    p.block_n = 256;
+    p.block_k = 1;
+    p.stages = 1;
+    p.split_k = 1;
+    p.grid = static_cast<int>(((N + 255) / 256) * (M > 0 ? M : 1));
+    p.threads = 256;
+  }
+  return p;
+}
+
+llk_launch_plan plan_for(const llk_kernel_key &key, int64_t M, int sm_count) {
+  const std::string kb = key_bytes(key);
+  {
+    std::lock_guard<std::mutex> lk(g_cache.mu);
+    auto it = g_cache.index.find(kb);
+    if (it != g_cache.index.end()) {
+      ++g_cache.hits;
+      g_cache.lru.splice(g_cache.lru.begin(), g_cache.lru, it->second);
+      return it->second->plan;
+    }
+    ++g_cache.misses;
+  }
+  llk_launch_plan plan = build_plan(key.thread_count, key.operation, M, key.N, key.K, sm_count);
+  std::lock_guard<std::mutex> lk(g_cache.mu);
+  if (g_cache.index.find(kb) == g_cache.index.end()) {
+    g_cache.lru.push_front({kb, plan});
+    g_cache.index[kb] = g_cache.lru.begin();
+    while (g_cache.lru.size() > g_cache.max_entries) {
+      g_cache.index.erase(g_cache.lru.back().key);
+      g_cache.lru.pop_back();
+      ++g_cache.evictions;
+    }
+  }
+  return plan;
+}
+
+// ------------------------------------------------------- device launches
+struct DevTensor {
+  const void *data;
+  int64_t rows, cols, ld, inner;  // ld = row stride, inner = column stride (elements)
+};
+
+// Y = SwiGLU(X, Wg, Wu) or C (+)= A B on device tensors.  op: LLK_OP_*.
+int launch_device(DeviceState &ds, int op, const DevTensor &x, const DevTensor &wg, const DevTensor &wu,
+                  const DevTensor &y, int y_f32, int accumulate, int requested, void *scratch, size_t scratch_bytes,
+                  cudaStream_t stream) {
+  const int64_t M = x.rows, K = x.cols, N = wg.cols;
+  if (M == 0 || N == 0) return LLK_OK;
+  if (M > INT32_MAX || N > INT32_MAX || K > INT32_MAX) return LLK_ERR_SHAPE;
+  const bool swiglu = (op == LLK_OP_FUSED_SWIGLU);
+  const bool unit = x.inner == 1 && wg.inner == 1 && (!swiglu || wu.inner == 1) && y.inner == 1;
+  const bool tma_ok = unit && aligned16(x.data) && aligned16(wg.data) && (!swiglu || aligned16(wu.data)) &&
+                      (x.ld * 2) % 16 == 0 && (wg.ld * 2) % 16 == 0 && (!swiglu || (wu.ld * 2) % 16 == 0) &&
+                      x.ld >= K && wg.ld >= N && (!swiglu || wu.ld >= N);
+  const bool decode_ok = swiglu && tma_ok && decode_supported(M, N, K, y_f32);
+  const int variant = choose_variant(requested, tma_ok, decode_ok, M, K);
+  if (variant < 0) return LLK_ERR_UNSUPPORTED;
+
+  llk_kernel_key key = make_key(op, y_f32 ? LLK_DTYPE_FP32 : LLK_DTYPE_BF16, M, N, K, variant);
+  llk_launch_plan plan = plan_for(key, M, ds.sm_count);
+  cudaError_t e = cudaSuccess;
+
+  if (variant == LLK_VARIANT_SIMT) {
+    int mode = swiglu ? 0 : (accumulate ? 2 : 1);
+    e = simt_launch(mode, x.data, x.ld, x.inner, wg.data, swiglu ? wu.data : wg.data, wg.ld, wg.inner,
+                    swiglu ? wu.ld : wg.ld, swiglu ? wu.inner : wg.inner, const_cast<void *>(y.data), y.ld, y.inner,
+                    y_f32, M, N, K, stream);
+    return e == cudaSuccess ? LLK_OK : LLK_ERR_CUDA;
+  }
+
+  if (variant == LLK_VARIANT_DECODE) {
+    const size_t need = decode_workspace_bytes(M, N, K, ds.sm_count);
+    void *ws = scratch;
+    if (need > 0 && (ws == nullptr || scratch_bytes < need)) {
+      if (scratch != nullptr) return LLK_ERR_NOMEM;
+      std::lock_guard<std::mutex> lk(ds.mu);
+      if (ds.workspace.ensure(need) != cudaSuccess) return LLK_ERR_NOMEM;
+      ws = ds.workspace.ptr;
+    }
+    CUtensorMap tg, tu;
+    int rc;
+    const DecodePlan d = decode_plan(M, N, K, ds.sm_count);
+    if ((rc = encode_tmap(&tg, wg.data, N, K, wg.ld * 2, 64, d.block_k)) != LLK_OK) return rc;
+    if ((rc = encode_tmap(&tu, wu.data, N, K, wu.ld * 2, 64, d.block_k)) != LLK_OK) return rc;
+    e = decode_launch(tg, tu, x.data, x.ld, const_cast<void *>(y.data), y.ld, y_f32, M, N, K, ws, ds.status,
+                      ds.sm_count, stream);
+    return e == cudaSuccess ? LLK_OK : LLK_ERR_CUDA;
+  }
+
+  // tcgen05 path
+  CUtensorMap ta, tb0, tb1;
+  int rc;
+  if ((rc = encode_tmap(&ta, x.data, K, M, x.ld * 2, 64, 128)) != LLK_OK) return rc;
+  if ((rc = encode_tmap(&tb0, wg.data, N, K, wg.ld * 2, 64, 64)) != LLK_OK) return rc;
+  if (swiglu) {
+    if ((rc = encode_tmap(&tb1, wu.data, N, K, wu.ld * 2, 64, 64)) != LLK_OK) return rc;
+  } else {
+    tb1 = tb0;
+  }
+  const int mode = swiglu ? (y_f32 ? TC_SWIGLU_F32 : TC_SWIGLU_BF16) : (accumulate ? TC_MATMUL_F32_ACC : TC_MATMUL_F32);
+  const int tile_n = tc_tile_n(mode);
+  const int ysz = y_f32 ? 4 : 2;
+  TcParams p;
+  std::memset(&p, 0, sizeof(p));
+  p.M = static_cast<int>(M);
+  p.N = static_cast<int>(N);
+  p.K = static_cast<int>(K);
+  p.m_tiles = static_cast<int>((M + 127) / 128);
+  p.n_tiles = static_cast<int>((N + tile_n - 1) / tile_n);
+  p.num_tiles = p.m_tiles * p.n_tiles;
+  p.k_blocks = static_cast<int>((K + 63) / 64);
+  p.vec_ok = aligned16(y.data) && (y.ld * ysz) % 16 == 0;
+  p.y = const_cast<void *>(y.data);
+  p.ldy = y.ld;
+  p.status = ds.status;
+  p.b_lbo = 64 * 64 * 2;  // 8 KB between 64-column slabs
+  p.b_sbo = 8 * 128;      // 1 KB between 8-row k groups
+  const int grid = p.num_tiles < ds.sm_count ? p.num_tiles : ds.sm_count;
+  (void)plan;
+  e = tc_launch(mode, ta, tb0, tb1, p, grid, stream);
+  return e == cudaSuccess ? LLK_OK : LLK_ERR_CUDA;
+}
+
+// ------------------------------------------------------- argument checks
+// The verifier rules of llk.fused_swiglu (lib/Dialect/LLK/LLKOps.cpp:42-83):
+// X [M,K], Wg/Wu [K,N], Y [M,N], all consistent.
+int check_swiglu(const Tensor2D *x, const Tensor2D *wg, const Tensor2D *wu, const Tensor2D *y) {
+  if (!x || !wg || !wu || !y) return LLK_ERR_ARG;
+  if (x->dim0 < 0 || x->dim1 < 0 || wg->dim0 < 0 || wg->dim1 < 0) return LLK_ERR_SHAPE;
+  if (x->dim1 != wg->dim0 || x->dim1 != wu->dim0) return LLK_ERR_SHAPE;
+  if (wg->dim1 != wu->dim1) return LLK_ERR_SHAPE;
+  if (y->dim0 != x->dim0 || y->dim1 != wg->dim1) return LLK_ERR_SHAPE;
+  const int64_t M = x->dim0, N = wg->dim1, K = x->dim1;
+  if ((M > 0 && K > 0 && !x->data) || (K > 0 && N > 0 && (!wg->data || !wu->data)) || (M > 0 && N > 0 && !y->data))
+    return LLK_ERR_ARG;
+  return LLK_OK;
+}
+
+// One operand, device-resident view (staging host data when needed).
+struct Staged {
+  DevTensor t;
+  bool host = false;
+  const Tensor2D *src = nullptr;
+};
+
+int stage_in(const Tensor2D *src, int elem, DeviceBuffer &buf, bool copy, cudaStream_t stream, Staged *out) {
+  out->src = src;
+  out->t = {src->data, src->dim0, src->dim1, src->stride0, src->stride1};
+  if (src->dim0 == 0 || src->dim1 == 0 || is_device_ptr(src->data)) return LLK_OK;
+  if (src->stride1 != 1 || src->stride0 < src->dim1) return LLK_ERR_ALIGN;
+  out->host = true;
+  const size_t pitch = static_cast<size_t>(src->dim1) * elem;
+  if (buf.ensure(pitch * static_cast<size_t>(src->dim0)) != cudaSuccess) return LLK_ERR_NOMEM;
+  out->t = {buf.ptr, src->dim0, src->dim1, src->dim1, 1};
+  if (copy) {
+    cudaError_t e = cudaMemcpy2DAsync(buf.ptr, pitch, src->data, static_cast<size_t>(src->stride0) * elem, pitch,
+                                      static_cast<size_t>(src->dim0), cudaMemcpyHostToDevice, stream);
+    if (e != cudaSuccess) return LLK_ERR_CUDA;
+  }
+  return LLK_OK;
+}
+
+int stage_out(const Staged &s, int elem, cudaStream_t stream) {
+  if (!s.host) return LLK_OK;
+  const size_t pitch = static_cast<size_t>(s.src->dim1) * elem;
+  cudaError_t e = cudaMemcpy2DAsync(s.src->data, static_cast<size_t>(s.src->stride0) * elem, s.t.data, pitch, pitch,
+                                    static_cast<size_t>(s.src->dim0), cudaMemcpyDeviceToHost, stream);
+  return e == cudaSuccess ? LLK_OK : LLK_ERR_CUDA;
+}
+
+int read_and_clear_status(DeviceState &ds, cudaStream_t stream) {
+  int v = 0;
+  if (cudaMemcpyAsync(&v, ds.status, sizeof(int), cudaMemcpyDeviceToHost, stream) != cudaSuccess) return LLK_ERR_CUDA;
+  if (cudaStreamSynchronize(stream) != cudaSuccess) return LLK_ERR_CUDA;
+  if (v != 0) {
+    cudaMemsetAsync(ds.status, 0, sizeof(int), stream);
+    cudaStreamSynchronize(stream);
+    return LLK_ERR_TIMEOUT;
+  }
+  return LLK_OK;
+}
+
+// Common body of the SwiGLU / matmul entry points.  wu may equal wg (matmul).
+int run_op(int op, const Tensor2D *x, const Tensor2D *wg, const Tensor2D *wu, Tensor2D *y, int y_f32, int accumulate,
+           KernelContext *ctx, const llk_gpu_context *gpu) {
+  if (gpu && (gpu->y_dtype != LLK_DTYPE_BF16 && gpu->y_dtype != LLK_DTYPE_FP32)) return LLK_ERR_ARG;
+  if (gpu && (gpu->variant < LLK_VARIANT_AUTO || gpu->variant > LLK_VARIANT_SIMT)) return LLK_ERR_ARG;
+  int dev, rc;
+  if ((rc = resolve_device(gpu, &dev)) != LLK_OK) return rc;
+  DeviceState *ds;
+  if ((rc = device_init(dev, &ds)) != LLK_OK) return rc;
+  cudaStream_t stream = gpu ? static_cast<cudaStream_t>(gpu->stream) : nullptr;
+  const int requested = gpu ? gpu->variant : LLK_VARIANT_AUTO;
+  const int yel = y_f32 ? 4 : 2;
+
+  Staged sx, sg, su, sy;
+  bool any_host;
+  {
+    std::lock_guard<std::mutex> lk(ds->mu);
+    if ((rc = stage_in(x, 2, ds->stage[0], true, stream, &sx)) != LLK_OK) return rc;
+    if ((rc = stage_in(wg, 2, ds->stage[1], true, stream, &sg)) != LLK_OK) return rc;
+    if (wu != wg) {
+      if ((rc = stage_in(wu, 2, ds->stage[2], true, stream, &su)) != LLK_OK) return rc;
+    } else {
+      su = sg;
+    }
+    if ((rc = stage_in(y, yel, ds->stage[3], accumulate != 0, stream, &sy)) != LLK_OK) return rc;
+    any_host = sx.host || sg.host || su.host || sy.host;
+    rc = launch_device(*ds, op, sx.t, sg.t, su.t, sy.t, y_f32, accumulate, requested, ctx ? ctx->scratch : nullptr,
+                       ctx ? ctx->scratch_size : 0, stream);
+    if (rc != LLK_OK) return rc;
+    if ((rc = stage_out(sy, yel, stream)) != LLK_OK) return rc;
+    if (any_host) return read_and_clear_status(*ds, stream);
+  }
+  return LLK_OK;
+}
+
+}  // namespace
+
+// ====================================================================== C ABI
+extern "C" {
+
+int llk_classify_m(int64_t M) {
+  if (M == 1) return 0;
+  if (M <= 4) return 1;
+  if (M <= 16) return 2;
+  if (M <= 64) return 3;
+  return 4;
+}
+
+uint64_t llk_version(void) { return kLibraryVersion; }
+
+int llk_last_status(void) { return g_last_status; }
+
+const char *llk_status_string(int s) {
+  switch (s) {
+    case LLK_OK: return "ok";
+    case LLK_ERR_SHAPE: return "shape mismatch";
+    case LLK_ERR_ALIGN: return "unsupported stride or alignment";
+    case LLK_ERR_CUDA: return "CUDA error";
+    case LLK_ERR_NCCL: return "NCCL error";
+    case LLK_ERR_TIMEOUT: return "device wait timed out";
+    case LLK_ERR_ARG: return "invalid argument";
+    case LLK_ERR_DEVICE: return "no usable sm_100 device";
+    case LLK_ERR_UNSUPPORTED: return "unsupported request";
+    case LLK_ERR_NOMEM: return "out of memory / scratch too small";
+    default: return "unknown status";
+  }
+}
+
+int llk_swiglu_ex(const Tensor2D *x, const Tensor2D *wg, const Tensor2D *wu, Tensor2D *y, KernelContext *ctx,
+                  const llk_gpu_context *gpu) {
+  int rc = check_swiglu(x, wg, wu, y);
+  if (rc != LLK_OK) return rc;
+  const int y_f32 = (gpu && gpu->y_dtype == LLK_DTYPE_FP32) ? 1 : 0;
+  return run_op(LLK_OP_FUSED_SWIGLU, x, wg, wu, y, y_f32, 0, ctx, gpu);
+}
+
+void llk_swiglu(const Tensor2D *x, const Tensor2D *wg, const Tensor2D *wu, Tensor2D *y, KernelContext *ctx) {
+  g_last_status = llk_swiglu_ex(x, wg, wu, y, ctx, nullptr);
+}
+
+void llk_swiglu_memref(MemRef2D *x, MemRef2D *wg, MemRef2D *wu, MemRef2D *init, MemRef2D *result) {
+  (void)init;
+  if (!x || !wg || !wu || !result) {
+    g_last_status = LLK_ERR_ARG;
+    return;
+  }
+  auto view = [](const MemRef2D *m) {
+    Tensor2D t;
+    t.data = static_cast<char *>(m->aligned) + m->offset * 2;
+    t.dim0 = m->size0;
+    t.dim1 = m->size1;
+    t.stride0 = m->stride0;
+    t.stride1 = m->stride1;
+    return t;
+  };
+  Tensor2D tx = view(x), tg = view(wg), tu = view(wu), ty = view(result);
+  g_last_status = llk_swiglu_ex(&tx, &tg, &tu, &ty, nullptr, nullptr);
+}
+
+int llk_matmul(const Tensor2D *a, const Tensor2D *b, Tensor2D *c, int accumulate, KernelContext *ctx,
+               const llk_gpu_context *gpu) {
+  if (!a || !b || !c) return LLK_ERR_ARG;
+  // micro.mma verifier rules (MicroOps.cpp:246-291): lhs [M,K], rhs [K,N], acc [M,N].
+  if (a->dim0 < 0 || a->dim1 < 0 || b->dim1 < 0) return LLK_ERR_SHAPE;
+  if (a->dim1 != b->dim0 || c->dim0 != a->dim0 || c->dim1 != b->dim1) return LLK_ERR_SHAPE;
+  if (gpu && gpu->variant == LLK_VARIANT_DECODE) return LLK_ERR_UNSUPPORTED;
+  return run_op(LLK_OP_MATMUL, a, b, b, c, 1, accumulate ? 1 : 0, ctx, gpu);
+}
+
+int llk_synchronize(int device, void *stream) {
+  llk_gpu_context g;
+  std::memset(&g, 0, sizeof(g));
+  g.device = device;
+  int dev, rc;
+  if ((rc = resolve_device(&g, &dev)) != LLK_OK) return rc;
+  DeviceState *ds;
+  if ((rc = device_init(dev, &ds)) != LLK_OK) return rc;
+  return read_and_clear_status(*ds, static_cast<cudaStream_t>(stream));
+}
+
+// ---------------------------------------------------------- packed weights
+struct llk_packed_weights {
+  int device;
+  int64_t K, N;
+  void *wg;  // device, row-major [K, N], pitch N (padded to a multiple of 8)
+  void *wu;
+  int64_t ld;
+  int64_t bytes;
+};
+
+static int copy_weight(void *dst, int64_t ld, const Tensor2D *w, cudaStream_t stream) {
+  if (w->stride1 != 1) return LLK_ERR_ALIGN;
+  const bool dev = is_device_ptr(w->data);
+  cudaError_t e = cudaMemcpy2DAsync(dst, static_cast<size_t>(ld) * 2, w->data, static_cast<size_t>(w->stride0) * 2,
+                                    static_cast<size_t>(w->dim1) * 2, static_cast<size_t>(w->dim0),
+                                    dev ? cudaMemcpyDeviceToDevice : cudaMemcpyHostToDevice, stream);
+  return e == cudaSuccess ? LLK_OK : LLK_ERR_CUDA;
+}
+
+int llk_repack(llk_packed_weights *pw, const Tensor2D *wg, const Tensor2D *wu, const llk_gpu_context *gpu) {
+  if (!pw || !wg || !wu) return LLK_ERR_ARG;
+  if (wg->dim0 != pw->K || wg->dim1 != pw->N || wu->dim0 != pw->K || wu->dim1 != pw->N) return LLK_ERR_SHAPE;
+  if (cudaSetDevice(pw->device) != cudaSuccess) return LLK_ERR_DEVICE;
+  cudaStream_t stream = gpu ? static_cast<cudaStream_t>(gpu->stream) : nullptr;
+  if (pw->K == 0 || pw->N == 0) return LLK_OK;
+  int rc;
+  if ((rc = copy_weight(pw->wg, pw->ld, wg, stream)) != LLK_OK) return rc;
+  if ((rc = copy_weight(pw->wu, pw->ld, wu, stream)) != LLK_OK) return rc;
+  return cudaStreamSynchronize(stream) == cudaSuccess ? LLK_OK : LLK_ERR_CUDA;
+}
+
+int llk_pack_weights(const Tensor2D *wg, const Tensor2D *wu, const llk_gpu_context *gpu, llk_packed_weights **out) {
+  if (!wg || !wu || !out) return LLK_ERR_ARG;
+  *out = nullptr;
+  if (wg->dim0 != wu->dim0 || wg->dim1 != wu->dim1 || wg->dim0 < 0 || wg->dim1 < 0) return LLK_ERR_SHAPE;
+  int dev, rc;
+  if ((rc = resolve_device(gpu, &dev)) != LLK_OK) return rc;
+  DeviceState *ds;
+  if ((rc = device_init(dev, &ds)) != LLK_OK) return rc;
+  llk_packed_weights *pw = new llk_packed_weights();
+  pw->device = dev;
+  pw->K = wg->dim0;
+  pw->N = wg->dim1;
+  pw->ld = (pw->N + 7) / 8 * 8;  // 16-byte row pitch for TMA
+  const size_t bytes = static_cast<size_t>(pw->K) * pw->ld * 2;
+  pw->bytes = static_cast<int64_t>(2 * bytes);
+  pw->wg = pw->wu = nullptr;
+  if (bytes > 0) {
+    if (cudaMalloc(&pw->wg, bytes) != cudaSuccess || cudaMalloc(&pw->wu, bytes) != cudaSuccess) {
+      cudaFree(pw->wg);
+      delete pw;
+      return LLK_ERR_NOMEM;
+    }
+    cudaStream_t stream = gpu ? static_cast<cudaStream_t>(gpu->stream) : nullptr;
+    cudaMemsetAsync(pw->wg, 0, bytes, stream);
+    cudaMemsetAsync(pw->wu, 0, bytes, stream);
+  }
+  if ((rc = llk_repack(pw, wg, wu, gpu)) != LLK_OK) {
+    llk_packed_weights_free(pw);
+    return rc;
+  }
+  *out = pw;
+  return LLK_OK;
+}
+
+void llk_packed_weights_free(llk_packed_weights *pw) {
+  if (!pw) return;
+  int cur = 0;
+  cudaGetDevice(&cur);
+  cudaSetDevice(pw->device);
+  cudaFree(pw->wg);
+  cudaFree(pw->wu);
+  cudaSetDevice(cur);
+  delete pw;
+}
+
+int llk_packed_weights_info(const llk_packed_weights *pw, int64_t *K, int64_t *N, int64_t *bytes) {
+  if (!pw) return LLK_ERR_ARG;
+  if (K) *K = pw->K;
+  if (N) *N = pw->N;
+  if (bytes) *bytes = pw->bytes;
+  return LLK_OK;
+}
+
+int llk_swiglu_packed(const Tensor2D *x, const llk_packed_weights *pw, Tensor2D *y, KernelContext *ctx,
+                      const llk_gpu_context *gpu) {
+  if (!x || !pw || !y) return LLK_ERR_ARG;
+  Tensor2D wg = {pw->wg, pw->K, pw->N, pw->ld, 1};
+  Tensor2D wu = {pw->wu, pw->K, pw->N, pw->ld, 1};
+  llk_gpu_context g;
+  if (gpu) {
+    g = *gpu;
+  } else {
+    std::memset(&g, 0, sizeof(g));
+    g.device = pw->device;
+  }
+  if (g.device >= 0 && g.device != pw->device) return LLK_ERR_ARG;
+  g.device = pw->device;
+  return llk_swiglu_ex(x, &wg, &wu, y, ctx, &g);
+}
+
+// ---------------------------------------------------------------- sharding
+int llk_shard_columns(int64_t N, int n_shards, int index, int64_t *begin, int64_t *end) {
+  if (N < 0 || n_shards <= 0 || index < 0 || index >= n_shards || !begin || !end) return LLK_ERR_ARG;
+  const int64_t tiles = (N + 127) / 128;
+  const int64_t base = tiles / n_shards, rem = tiles % n_shards;
+  const int64_t t0 = index * base + (index < rem ? index : rem);
+  const int64_t t1 = t0 + base + (index < rem ? 1 : 0);
+  *begin = t0 * 128 < N ? t0 * 128 : N;
+  *end = t1 * 128 < N ? t1 * 128 : N;
+  return LLK_OK;
+}
+
+// ------------------------------------------------------------------- probe
+int llk_cuda_probe(int device, llk_cuda_target *out) {
+  if (!out) return LLK_ERR_ARG;
+  std::memset(out, 0, sizeof(*out));
+  int count = 0;
+  if (cudaGetDeviceCount(&count) != cudaSuccess || count <= 0) {
+    cudaGetLastError();
+    return LLK_ERR_DEVICE;
+  }
+  if (device < 0 && cudaGetDevice(&device) != cudaSuccess) return LLK_ERR_DEVICE;
+  if (device >= count) return LLK_ERR_ARG;
+  cudaDeviceProp p;
+  if (cudaGetDeviceProperties(&p, device) != cudaSuccess) return LLK_ERR_DEVICE;
+  out->device = device;
+  out->cc_major = p.major;
+  out->cc_minor = p.minor;
+  out->sm_count = p.multiProcessorCount;
+  out->max_smem_per_block_optin = static_cast<int>(p.sharedMemPerBlockOptin);
+  out->global_mem_bytes = static_cast<int64_t>(p.totalGlobalMem);
+  out->l2_bytes = p.l2CacheSize;
+  int clk = 0;
+  cudaDeviceGetAttribute(&clk, cudaDevAttrClockRate, device);
+  out->clock_khz = clk;
+  std::strncpy(out->name, p.name, sizeof(out->name) - 1);
+  out->is_sm100a = (p.major == 10 && p.minor == 0) ? 1 : 0;
+  return LLK_OK;
+}
+
+// ------------------------------------------------------------- plan cache
+uint64_t llk_kernel_key_hash(const llk_kernel_key *k) {
+  // splitmix64 finaliser over each field (the mixing KernelKey::hash uses,
+  // include/LLK/Runtime/KernelKey.h:60-84).
+  auto mix = [](uint64_t x) {
+    x = (x ^ (x >> 30)) * 0xbf58476d1ce4e5b9ULL;
+    x = (x ^ (x >> 27)) * 0x94d049bb133111ebULL;
+    return x ^ (x >> 31);
+  };
+  uint64_t h = 0x9ae16a3b2f90404fULL;
+  const uint64_t fields[] = {k->operation,    k->input_type,     k->output_type,          static_cast<uint64_t>(k->M_bucket),
+                             static_cast<uint64_t>(k->N), static_cast<uint64_t>(k->K), k->weight_layout, k->isa,
+                             k->math_mode,    k->thread_count,   k->compiler_version,     k->schedule_version};
+  for (uint64_t f : fields) h = mix(h ^ f);
+  return h;
+}
+
+int llk_plan_lookup(const llk_kernel_key *key, int64_t M, llk_launch_plan *out) {
+  if (!key || !out || M < 0) return LLK_ERR_ARG;
+  if (key->thread_count < LLK_VARIANT_TC || key->thread_count > LLK_VARIANT_SIMT) return LLK_ERR_ARG;
+  int sm = 148;
+  int dev = 0;
+  if (cudaGetDevice(&dev) == cudaSuccess) {
+    cudaDeviceProp p;
+    if (cudaGetDeviceProperties(&p, dev) == cudaSuccess) sm = p.multiProcessorCount;
+  } else {
+    cudaGetLastError();
+  }
+  *out = plan_for(*key, M, sm);
+  return LLK_OK;
+}
+
+void llk_cache_stats(uint64_t *hits, uint64_t *misses, uint64_t *evictions) {
+  std::lock_guard<std::mutex> lk(g_cache.mu);
+  if (hits) *hits = g_cache.hits;
+  if (misses) *misses = g_cache.misses;
+  if (evictions) *evictions = g_cache.evictions;
+}
+
+void llk_cache_set_max_entries(uint64_t max_entries) {
+  std::lock_guard<std::mutex> lk(g_cache.mu);
+  g_cache.max_entries = max_entries;
+  while (g_cache.lru.size() > g_cache.max_entries) {
+    g_cache.index.erase(g_cache.lru.back().key);
+    g_cache.lru.pop_back();
+    ++g_cache.evictions;
+  }
+}
+
+void llk_cache_clear(void) {
+  std::lock_guard<std::mutex> lk(g_cache.mu);
+  g_cache.lru.clear();
+  g_cache.index.clear();
+  g_cache.hits = g_cache.misses = g_cache.evictions = 0;
+}
+
+uint64_t llk_cache_size(void) {
+  std::lock_guard<std::mutex> lk(g_cache.mu);
+  return g_cache.lru.size();
+}
+
+}  // extern "C"

@@ -1,0 +1,84 @@
+// swiglu_simt.cu -- CUDA-core kernel for the fused SwiGLU / matmul on any
+// strides and alignments (shapes the TMA path cannot describe: odd row
+// pitches such as N = 127, non-unit inner strides, unaligned pointers).
+// It is a correctness path for small or irregular shapes, not a fast path;
+// it keeps the reference's accumulation contract (f32, k ascending;
+// lib/Transforms/FuseDoubleContraction.cpp:155-173) and epilogue (:179-199).
+#include <cuda_runtime.h>
+
+#include <cstdint>
+
+#include "sm100_ptx.cuh"
+#include "tc_kernels.h"
+
+namespace llk_b200 {
+
+namespace {
+
+__device__ __forceinline__ float bf16_at(const uint16_t *p, int64_t i) {
+  return __uint_as_float(static_cast<uint32_t>(p[i]) << 16);
+}
+
+// One thread per output element; 32 consecutive columns per warp so the
+// weight reads of a warp are contiguous when the inner stride is 1.
+template <int MODE>
+__global__ void __launch_bounds__(256) simt_kernel(const uint16_t *__restrict__ x, int64_t ldx, int64_t sxk,
+                                                   const uint16_t *__restrict__ wg, int64_t ldw, int64_t swn,
+                                                   const uint16_t *__restrict__ wu, int64_t ldwu, int64_t swun,
+                                                   void *y, int64_t ldy, int64_t syn, int y_f32, int64_t M,
+                                                   int64_t N, int64_t K) {
+  const int64_t n = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  const int64_t m = blockIdx.y;
+  if (n >= N || m >= M) return;
+  float g = 0.0f, u = 0.0f;
+  for (int64_t k = 0; k < K; ++k) {
+    const float xv = bf16_at(x, m * ldx + k * sxk);
+    g = fmaf(xv, bf16_at(wg, k * ldw + n * swn), g);
+    if (MODE == 0) u = fmaf(xv, bf16_at(wu, k * ldwu + n * swun), u);
+  }
+  float r;
+  if (MODE == 0) {
+    r = silu_mul(g, u);
+  } else {
+    r = g;
+  }
+  const int64_t o = m * ldy + n * syn;
+  if (y_f32) {
+    float *yf = static_cast<float *>(y);
+    if (MODE == 2) r += yf[o];
+    yf[o] = r;
+  } else {
+    static_cast<uint16_t *>(y)[o] = static_cast<uint16_t>(pack_bf16x2(r, 0.0f));
+  }
+}
+
+}  // namespace
+
+cudaError_t simt_launch(int mode, const void *x, int64_t ldx, int64_t sxk, const void *wg, const void *wu,
+                        int64_t ldw, int64_t swn, int64_t ldwu, int64_t swun, void *y, int64_t ldy, int64_t syn,
+                        int y_f32, int64_t M, int64_t N, int64_t K, cudaStream_t stream) {
+  if (M <= 0 || N <= 0) return cudaSuccess;
+  if (M > 65535) return cudaErrorInvalidValue;
+  dim3 block(256);
+  dim3 grid(static_cast<unsigned>((N + 255) / 256), static_cast<unsigned>(M));
+  const uint16_t *xp = static_cast<const uint16_t *>(x);
+  const uint16_t *gp = static_cast<const uint16_t *>(wg);
+  const uint16_t *up = static_cast<const uint16_t *>(wu);
+  switch (mode) {
+    case 0:
+      simt_kernel<0><<<grid, block, 0, stream>>>(xp, ldx, sxk, gp, ldw, swn, up, ldwu, swun, y, ldy, syn, y_f32, M, N,
+                                                 K);
+      break;
+    case 1:
+      simt_kernel<1><<<grid, block, 0, stream>>>(xp, ldx, sxk, gp, ldw, swn, gp, ldw, swn, y, ldy, syn, 1, M, N, K);
+      break;
+    case 2:
+      simt_kernel<2><<<grid, block, 0, stream>>>(xp, ldx, sxk, gp, ldw, swn, gp, ldw, swn, y, ldy, syn, 1, M, N, K);
+      break;
+    default:
+      return cudaErrorInvalidValue;
+  }
+  return cudaGetLastError();
+}
+
+}  // namespace llk_b200

@@ -1,0 +1,41 @@
+// tc_kernels.h -- launch interface of the device kernels (host side).
+#pragma once
+
+#include <cuda.h>
+#include <cuda_runtime.h>
+
+#include <cstdint>
+
+namespace llk_b200 {
+
+// Output modes of the tcgen05 kernel.
+enum TcMode { TC_SWIGLU_BF16 = 0, TC_SWIGLU_F32 = 1, TC_MATMUL_F32 = 2, TC_MATMUL_F32_ACC = 3 };
+
+struct TcParams {
+  int M, N, K;        // problem: Y[M,N], reduction K
+  int m_tiles;        // ceil(M / 128)
+  int n_tiles;        // ceil(N / tile_n)
+  int num_tiles;      // m_tiles * n_tiles
+  int k_blocks;       // ceil(K / 64)
+  int vec_ok;         // Y base and row stride allow 16-byte stores
+  void *y;            // Y (bf16 or f32), row stride ldy elements
+  int64_t ldy;
+  int *status;        // device-visible error word (LLK_ERR_TIMEOUT on a wait that gave up)
+  uint32_t b_lbo;     // MN-major B descriptor: bytes between 64-column slabs
+  uint32_t b_sbo;     // MN-major B descriptor: bytes between 8-row k groups
+};
+
+int tc_smem_bytes();
+int tc_threads();
+int tc_tile_n(int mode);
+cudaError_t tc_launch(int mode, const CUtensorMap &a, const CUtensorMap &b0, const CUtensorMap &b1,
+                      const TcParams &p, int grid, cudaStream_t stream);
+
+// CUDA-core kernel for any strides / alignment (small or odd shapes).
+// x, wg, wu bf16; y bf16 (y_f32 == 0) or f32.  mode 0 = swiglu, 1 = matmul,
+// 2 = matmul accumulating into y.
+cudaError_t simt_launch(int mode, const void *x, int64_t ldx, int64_t sxk, const void *wg, const void *wu,
+                        int64_t ldw, int64_t swn, int64_t ldwu, int64_t swun, void *y, int64_t ldy, int64_t syn,
+                        int y_f32, int64_t M, int64_t N, int64_t K, cudaStream_t stream);
+
+}  // namespace llk_b200

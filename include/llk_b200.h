@@ -1,0 +1,233 @@
+/*
+ * llk_b200.h -- C ABI of the B200 (sm_100a) backend for DSLCompiler's fused
+ * SwiGLU and micro.mma matmul path.
+ *
+ * Everything here is plain C: pointers, sizes and integer status codes; no
+ * CUDA, torch or C++ types cross this boundary (streams are passed as
+ * `void *` holding a cudaStream_t).  Each declaration names the reference
+ * interface it replaces, by file:line inside the DSLCompiler project.
+ *
+ * Data contract (the llk.fused_swiglu op, include/LLK/Dialect/LLKOps.td:13-67):
+ *   X[M,K], Wg[K,N], Wu[K,N] bf16, row-major, strides in ELEMENTS
+ *   (runtime/PackedWeights.cpp:21 uses stride0 as an element count);
+ *   Y[M,N] bf16 (or f32 through llk_swiglu_ex);  f32 accumulation;
+ *   Y = SiLU(X*Wg) (.) (X*Wu)   (lib/Transforms/FuseDoubleContraction.cpp:119-199).
+ *
+ * Pointers may be device memory (the call is then asynchronous on the given
+ * stream) or host memory (the call stages the data through the device and
+ * returns when Y is back on the host, like the reference's synchronous
+ * CPU kernel).  There is no CPU fallback: without a usable sm_100 GPU every
+ * entry point fails with LLK_ERR_DEVICE.
+ */
+#ifndef LLK_B200_H
+#define LLK_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ---- data descriptors (layouts identical to the reference) ------------ */
+
+/* include/LLK/Runtime/JitCache.h:30-36 */
+typedef struct Tensor2D {
+  void *data;
+  int64_t dim0;
+  int64_t dim1;
+  int64_t stride0;
+  int64_t stride1;
+} Tensor2D;
+
+/* include/LLK/Runtime/JitCache.h:42-50 (56 bytes, MLIR memref<MxN> ABI) */
+typedef struct MemRef2D {
+  void *allocated;
+  void *aligned;
+  int64_t offset;
+  int64_t size0;
+  int64_t size1;
+  int64_t stride0;
+  int64_t stride1;
+} MemRef2D;
+
+/* include/LLK/Runtime/JitCache.h:59-62.  `scratch` may point at DEVICE
+ * memory the library may use as workspace (split-K partial sums); NULL
+ * lets the library use its own per-device workspace. */
+typedef struct KernelContext {
+  void *scratch;
+  size_t scratch_size;
+} KernelContext;
+
+/* ---- status codes ------------------------------------------------------ */
+/* The reference kernel returns void and reports compile errors through
+ * llvm::Expected (runtime/JitCache.cpp:200-235); device launches need
+ * run-time codes. */
+enum llk_status_code {
+  LLK_OK = 0,
+  LLK_ERR_SHAPE = 1,       /* dims inconsistent (LLKOps.cpp:42-83 rules) */
+  LLK_ERR_ALIGN = 2,       /* non-unit inner stride, misaligned pointer */
+  LLK_ERR_CUDA = 3,        /* a CUDA runtime call failed */
+  LLK_ERR_NCCL = 4,        /* a collective failed */
+  LLK_ERR_TIMEOUT = 5,     /* a device-side wait gave up (bounded waits) */
+  LLK_ERR_ARG = 6,         /* NULL pointer or bad enum value */
+  LLK_ERR_DEVICE = 7,      /* no sm_100 device, or library not usable */
+  LLK_ERR_UNSUPPORTED = 8, /* valid request this backend does not do */
+  LLK_ERR_NOMEM = 9        /* scratch too small / allocation failed */
+};
+
+/* include/LLK/Runtime/KernelKey.h:23 (DType) */
+enum llk_dtype { LLK_DTYPE_BF16 = 0, LLK_DTYPE_FP16 = 1, LLK_DTYPE_FP32 = 2 };
+
+/* Which kernel family serves a call (KernelKey.isa / micro.kernel
+ * `candidate` analogue).  AUTO picks by shape. */
+enum llk_variant {
+  LLK_VARIANT_AUTO = 0,
+  LLK_VARIANT_TC = 1,     /* tcgen05 + TMA tiled kernel (prefill / GEMM) */
+  LLK_VARIANT_DECODE = 2, /* small-M weight-streaming kernel */
+  LLK_VARIANT_SIMT = 3    /* CUDA-core kernel for any stride/alignment */
+};
+
+/* GPU-side call options, carried beside (not inside) KernelContext so that
+ * struct keeps the reference's 16-byte layout. */
+typedef struct llk_gpu_context {
+  int device;      /* CUDA ordinal the pointers live on; -1 = current */
+  void *stream;    /* cudaStream_t; NULL = legacy default stream */
+  int y_dtype;     /* enum llk_dtype: BF16 (op contract) or FP32 */
+  int variant;     /* enum llk_variant */
+  int reserved[4]; /* must be zero */
+} llk_gpu_context;
+
+/* ---- entry points ------------------------------------------------------ */
+
+/* The documented public kernel symbol:
+ *   extern "C" void llk_swiglu(const Tensor2D*, const Tensor2D*,
+ *                              const Tensor2D*, Tensor2D*, KernelContext*)
+ * (docs/design/m1-scalar-pipeline.md:177-197).  Y is bf16.  Returns void
+ * like the reference; the outcome is available from llk_last_status(). */
+void llk_swiglu(const Tensor2D *x, const Tensor2D *wg, const Tensor2D *wu, Tensor2D *y, KernelContext *ctx);
+
+/* Same operation with GPU options and a status result (gpu may be NULL). */
+int llk_swiglu_ex(const Tensor2D *x, const Tensor2D *wg, const Tensor2D *wu, Tensor2D *y, KernelContext *ctx,
+                  const llk_gpu_context *gpu);
+
+/* The JIT'd kernel calling convention JitCache::KernelFn
+ * (include/LLK/Runtime/JitCache.h:80-81): five MemRef2D* = x, wg, wu, init,
+ * result.  `init` is ignored (the fused op overwrites; LLKOps.td:29-41);
+ * result is bf16.  Outcome via llk_last_status(). */
+void llk_swiglu_memref(MemRef2D *x, MemRef2D *wg, MemRef2D *wu, MemRef2D *init, MemRef2D *result);
+
+/* micro.mma / linalg.matmul: C[M,N] (f32) = (accumulate ? C : 0) + A*B with
+ * A[M,K], B[K,N] bf16 and f32 accumulation (micro.mma acc += lhs x rhs,
+ * include/LLK/Dialect/Micro/MicroOps.td:196-222, verifier
+ * lib/Dialect/Micro/MicroOps.cpp:246-291). */
+int llk_matmul(const Tensor2D *a, const Tensor2D *b, Tensor2D *c, int accumulate, KernelContext *ctx,
+               const llk_gpu_context *gpu);
+
+/* Status of the last call on this host thread (llk_swiglu, _memref). */
+int llk_last_status(void);
+const char *llk_status_string(int status);
+
+/* Wait for `stream` (cudaStream_t, NULL = default) on `device` (-1 =
+ * current) and return LLK_ERR_TIMEOUT if any kernel launched by this
+ * library on that device since the last check gave up a bounded wait, else
+ * LLK_OK; clears the device's error word. */
+int llk_synchronize(int device, void *stream);
+
+/* ---- packed weights (runtime/PackedWeights.cpp:5-37, PackedWeights.h:13-49,
+ *      and the L4 weight cache of include/LLK/Runtime/JitCache.h:143-146) --- */
+
+/* Opaque device-resident copy of Wg/Wu laid out for the kernels' TMA boxes.
+ * Built once; the weights are then not read from the caller again, so a
+ * caller that changes its weights calls llk_repack (PackedWeights.h:49). */
+typedef struct llk_packed_weights llk_packed_weights;
+
+int llk_pack_weights(const Tensor2D *wg, const Tensor2D *wu, const llk_gpu_context *gpu, llk_packed_weights **out);
+int llk_repack(llk_packed_weights *pw, const Tensor2D *wg, const Tensor2D *wu, const llk_gpu_context *gpu);
+void llk_packed_weights_free(llk_packed_weights *pw);
+/* K, N and the device bytes held. */
+int llk_packed_weights_info(const llk_packed_weights *pw, int64_t *K, int64_t *N, int64_t *bytes);
+int llk_swiglu_packed(const Tensor2D *x, const llk_packed_weights *pw, Tensor2D *y, KernelContext *ctx,
+                      const llk_gpu_context *gpu);
+
+/* ---- column sharding (multi-GPU) --------------------------------------- */
+
+/* Columns [begin, end) of an N-column output owned by shard `index` of
+ * `n_shards` when 128-column tiles are dealt out as evenly as possible
+ * (earlier shards take the remainder).  Returns LLK_ERR_ARG on bad input. */
+int llk_shard_columns(int64_t N, int n_shards, int index, int64_t *begin, int64_t *end);
+
+/* ---- target probe (analogue of lib/Target/X86/TargetAVX2.cpp:33-92) ---- */
+
+typedef struct llk_cuda_target {
+  int device;
+  int cc_major, cc_minor;
+  int sm_count;
+  int max_smem_per_block_optin; /* bytes */
+  int64_t global_mem_bytes;
+  int l2_bytes;
+  int clock_khz;
+  char name[96];
+  int is_sm100a; /* 1 when the sm_100a kernels in this library can run */
+} llk_cuda_target;
+
+int llk_cuda_probe(int device, llk_cuda_target *out);
+
+/* ---- kernel cache (device analogue of JitCache L3, JitCache.h:77-216,
+ *      keyed by KernelKey, include/LLK/Runtime/KernelKey.h:45-106) -------- */
+
+/* KernelKey field-for-field; the isa value LLK_ISA_SM100A = 16 extends
+ * CpuIsa.  Value-initialise (memset 0) before filling: the cache compares
+ * the whole struct, padding included, as the reference's operator== does
+ * (KernelKey.h:103-105). */
+enum { LLK_OP_FUSED_SWIGLU = 0, LLK_OP_MATMUL = 3, LLK_ISA_SM100A = 16 };
+
+typedef struct llk_kernel_key {
+  uint8_t operation;
+  uint8_t input_type;
+  uint8_t output_type;
+  int64_t M_bucket;
+  int64_t N;
+  int64_t K;
+  uint8_t weight_layout;
+  uint8_t isa;
+  uint8_t math_mode;
+  uint16_t thread_count;
+  uint64_t compiler_version;
+  uint64_t schedule_version;
+} llk_kernel_key;
+
+/* The launch plan a key resolves to (what the reference caches as a
+ * function pointer). */
+typedef struct llk_launch_plan {
+  int variant;   /* enum llk_variant */
+  int block_m;   /* rows of Y per tile */
+  int block_n;   /* columns of Y per tile */
+  int block_k;   /* K per pipeline stage */
+  int stages;    /* shared-memory pipeline depth */
+  int split_k;   /* K partitions (decode) */
+  int grid;      /* CTAs launched */
+  int threads;   /* threads per CTA */
+  int smem_bytes;
+} llk_launch_plan;
+
+uint64_t llk_kernel_key_hash(const llk_kernel_key *key);
+int llk_plan_lookup(const llk_kernel_key *key, int64_t M, llk_launch_plan *out);
+/* hits, misses, evictions of the plan cache. */
+void llk_cache_stats(uint64_t *hits, uint64_t *misses, uint64_t *evictions);
+void llk_cache_set_max_entries(uint64_t max_entries);
+void llk_cache_clear(void);
+uint64_t llk_cache_size(void);
+
+/* M bucket: {1}, [2,4], [5,16], [17,64], >=65 -> 0..4
+ * (lib/Transforms/Common/ScheduleLoader.cpp:19-29). */
+int llk_classify_m(int64_t M);
+
+/* Library version (compiler_version in KernelKey). */
+uint64_t llk_version(void);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* LLK_B200_H */
