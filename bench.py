@@ -1,0 +1,418 @@
+#!/usr/bin/env python
+"""Benchmark of the fused SwiGLU hot path on B200 (one JSON line on stdout).
+
+Workload (the configuration the headline metric is quoted on): Llama-7B
+prefill SwiGLU, X[2048,4096] x Wg,Wu[4096,11008] bf16, f32 accumulation,
+Y bf16.  One step = one launch of the fused kernel over the whole problem
+(at N GPUs: this rank's column shard, 128-column tiles dealt out evenly; no
+collective on the data path).  Inputs are seeded synthetic tensors of the
+configured shapes and distributions.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+    torchrun --nproc-per-node N bench.py --gpus N ...
+
+value: whole-job TFLOP/s = 4*M*N*K / (max over ranks of the summed
+per-step kernel times / K), inputs resident in HBM, L2 flushed (256 MiB
+write) before every timed step.  e2e: the same metric through the C ABI
+``llk_swiglu`` with pinned HOST buffers (H2D of X, Wg, Wu and D2H of Y in
+the timed region, every step).  --impl reference times the CPU restatement
+of the reference's fused AVX2 schedule on this host's cores instead.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import re
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+CONFIG = dict(name="c3", M=2048, K=4096, N=11008, x_std=1.0, w_std=0.02)
+METRIC = "fused SwiGLU BF16 TFLOP/s (Llama-7B prefill shape, config 3)"
+UNIT = "TFLOP/s"
+FLUSH_BYTES = 256 << 20
+
+
+def dist_env():
+    return int(os.environ.get("RANK", 0)), int(os.environ.get("LOCAL_RANK", 0)), int(os.environ.get("WORLD_SIZE", 1))
+
+
+def measured_peaks():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        with open(p) as f:
+            d = json.load(f)
+        return d.get("bf16_tflops"), d.get("hbm_gbs"), "measured"
+    return 1590.0, 6650.0, "fallback"
+
+
+def profile_traffic(name):
+    """dram bytes per launch recorded from an ncu capture in profiles/<name>.md
+    (a line 'traffic_bytes_per_launch: <int>')."""
+    p = os.path.join(ROOT, "profiles", name + ".md")
+    if not os.path.exists(p):
+        return None
+    m = re.search(r"traffic_bytes_per_launch:\s*([0-9.eE+]+)", open(p).read())
+    return float(m.group(1)) if m else None
+
+
+class ClockSampler:
+    """nvidia-smi clocks / throttle reasons sampled while the timed region runs."""
+    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,clocks_event_reasons.hw_slowdown,"
+         "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+         "clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpus):
+        self.gpus = set(gpus)
+        self.rows = []
+        self.proc = None
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", "--query-gpu=" + self.Q, "--format=csv,noheader,nounits",
+                                          "-lms", "100"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL,
+                                         text=True)
+            self.t = threading.Thread(target=self._read, daemon=True)
+            self.t.start()
+        except Exception:
+            self.proc = None
+        return self
+
+    def _read(self):
+        for line in self.proc.stdout:
+            f = [s.strip() for s in line.split(",")]
+            if len(f) == 9:
+                self.rows.append(f)
+
+    def __exit__(self, *a):
+        if self.proc:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except Exception:
+                self.proc.kill()
+
+    def summary(self):
+        rows = [r for r in self.rows if r[0].isdigit() and int(r[0]) in self.gpus]
+        if not rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [], "samples": 0}
+        sm = [float(r[1]) for r in rows if r[1].replace(".", "").isdigit()]
+        mx = [float(r[2]) for r in rows if r[2].replace(".", "").isdigit()]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for r in rows for i in range(4) if r[5 + i].lower() == "active"})
+        pw = [float(r[3]) for r in rows if re.match(r"^[0-9.]+$", r[3])]
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(mx) if mx else None,
+                "reasons": reasons, "samples": len(rows), "power_w_max": max(pw) if pw else None}
+
+
+def cpu_port_run(x, wg, wu, rows, threads):
+    import oracle
+
+    t0 = time.perf_counter()
+    oracle.port_swiglu(x[:rows], wg, wu, "bf16", threads=threads)
+    return time.perf_counter() - t0
+
+
+def cpu_baseline(x, wg, wu, budget_s=12.0):
+    """The threaded fused-schedule CPU port on this host, on a bounded row
+    sample of the workload, repeated for about `budget_s` seconds."""
+    import oracle
+
+    oracle.build()
+    threads = os.cpu_count() or 1
+    rows = 64
+    K, N = wg.shape
+    t = cpu_port_run(x, wg, wu, rows, threads)  # warm-up + size probe
+    times = []
+    t_end = time.perf_counter() + budget_s
+    while time.perf_counter() < t_end or not times:
+        times.append(cpu_port_run(x, wg, wu, rows, threads))
+    best = min(times)
+    return {"value": 4.0 * rows * N * K / best / 1e12, "unit": UNIT, "cores": threads, "kind": "port",
+            "sample": f"{rows} of {x.shape[0]} token rows x full N={N}, K={K}; best of {len(times)} runs "
+                      f"(~{sum(times) + t:.0f} s); oracle/swiglu_port.c fused schedule BM=32 BN=64 BK=64"}
+
+
+def reference_arm(args):
+    rank, _, world = dist_env()
+    if rank != 0:
+        return 0
+    from dslcompiler_b200 import datagen as dg
+    import oracle
+
+    oracle.build()
+    M, K, N = CONFIG["M"], CONFIG["K"], CONFIG["N"]
+    x, wg, wu = dg.swiglu_inputs(M, K, N, CONFIG["x_std"], CONFIG["w_std"], seed=42)
+    threads = os.cpu_count() or 1
+    rows = 32
+    for _ in range(args.warmup):
+        cpu_port_run(x, wg, wu, rows, threads)
+    times = [cpu_port_run(x, wg, wu, rows, threads) for _ in range(args.steps)]
+    mean = sum(times) / len(times)
+    value = 4.0 * rows * N * K / mean / 1e12
+    sample = (f"each step: {rows} of {M} token rows x full N={N}, K={K} (bounded sample of the workload); "
+              f"CPU restatement of the reference's fused AVX2 schedule (oracle/swiglu_port.c) on {threads} threads")
+    line = {"impl": "reference", "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": mean * 1e3 * M / rows,
+            "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
+            "data": "synthetic (seeded splitmix64/Box-Muller, X~N(0,1), W~N(0,0.02), bf16)",
+            "config": {"workload": "c3 llama7b-prefill swiglu", "M": M, "K": K, "N": N, "sample_rows": rows},
+            "cpu_baseline": {"value": value, "unit": UNIT, "cores": threads, "kind": "port", "sample": sample},
+            "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+            "note": "the reference's own path (MLIR/LLVM ORC JIT) cannot be built here; its naive test oracle is "
+                    "slower than this port, so the port is the faster, conservative CPU arm"}
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+def bf16_tensor(a_u16, pin=False):
+    import torch
+
+    t = torch.from_numpy(np.ascontiguousarray(a_u16).view(np.int16)).view(torch.bfloat16)
+    return t.pin_memory() if pin else t
+
+
+def time_steps(fn, flush, steps, stream):
+    """Per-step CUDA-event durations (ms) of fn(), L2 flushed before each."""
+    import torch
+
+    evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(steps)]
+    for s, e in evs:
+        if flush is not None:
+            flush()
+        s.record(stream)
+        fn()
+        e.record(stream)
+    torch.cuda.synchronize()
+    return [s.elapsed_time(e) for s, e in evs]
+
+
+def our_arm(args):
+    import torch
+    import torch.distributed as dist
+
+    import dslcompiler_b200 as llk
+    from dslcompiler_b200 import datagen as dg
+
+    rank, local, world = dist_env()
+    torch.cuda.set_device(local)
+    if world > 1:
+        dist.init_process_group("nccl", device_id=torch.device("cuda", local))
+    dev = torch.device("cuda", local)
+    stream = torch.cuda.current_stream(dev)
+
+    M, K, N = CONFIG["M"], CONFIG["K"], CONFIG["N"]
+    x, wg, wu = dg.swiglu_inputs(M, K, N, CONFIG["x_std"], CONFIG["w_std"], seed=42)
+    b, e = llk.shard_columns(N, world, rank)
+    n_r = e - b
+    wg_s = np.ascontiguousarray(wg[:, b:e])
+    wu_s = np.ascontiguousarray(wu[:, b:e])
+
+    xd, gd, ud = bf16_tensor(x).to(dev), bf16_tensor(wg_s).to(dev), bf16_tensor(wu_s).to(dev)
+    yd = torch.empty((M, n_r), dtype=torch.bfloat16, device=dev)
+    flush_buf = torch.empty(FLUSH_BYTES, dtype=torch.uint8, device=dev)
+
+    def flush():
+        flush_buf.zero_()
+
+    def step():
+        llk.fused_swiglu(xd, gd, ud, out=yd)
+
+    def barrier():
+        if world > 1:
+            dist.barrier(device_ids=[local])
+
+    def max_over_ranks(v):
+        if world == 1:
+            return v
+        t = torch.tensor([v], dtype=torch.float64, device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    def sum_over_ranks(v):
+        if world == 1:
+            return v
+        t = torch.tensor([v], dtype=torch.float64, device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.SUM)
+        return float(t.item())
+
+    # ---------------------------------------------------------- value
+    for _ in range(args.warmup):
+        flush()
+        step()
+    torch.cuda.synchronize()
+    llk.synchronize(local)
+    barrier()
+    torch.cuda.synchronize()
+    sampler = ClockSampler(range(world)) if local == 0 else None
+    if sampler:
+        sampler.__enter__()
+    t_wall0 = time.perf_counter()
+    times = time_steps(step, flush, args.steps, stream)
+    t_wall = time.perf_counter() - t_wall0
+    barrier()
+    torch.cuda.synchronize()
+    if sampler:
+        sampler.__exit__()
+    llk.synchronize(local)
+    kernel_ms = sum(times)
+    job_ms = max_over_ranks(kernel_ms) / args.steps
+    total_flops = 4.0 * M * N * K
+    value = total_flops / (job_ms * 1e-3) / 1e12
+
+    # ------------------------------------------------------- roofline
+    peak_tf, peak_gbs, peak_src = measured_peaks()
+    my_ms = kernel_ms / args.steps
+    achieved = 4.0 * M * n_r * K / (my_ms * 1e-3) / 1e12
+    traffic = profile_traffic("tc_swiglu_c3") if world == 1 else None
+
+    # ----------------------------------------------------------- e2e
+    # Through the reference-facing C ABI (llk_swiglu) with pinned host
+    # buffers: every step copies X, Wg, Wu (this rank's shard) in and Y out.
+    xh, gh, uh = bf16_tensor(x, pin=True), bf16_tensor(wg_s, pin=True), bf16_tensor(wu_s, pin=True)
+    yh = torch.empty((M, n_r), dtype=torch.bfloat16).pin_memory()
+    e2e_steps = max(3, min(args.steps, 30))
+    torch.cuda.set_device(local)
+
+    def e2e_step():
+        st = llk.swiglu_c_abi(xh, gh, uh, yh)
+        if st != 0:
+            raise RuntimeError(f"llk_swiglu failed: {st}")
+
+    for _ in range(2):
+        e2e_step()
+    barrier()
+    dstream = torch.cuda.default_stream(dev)
+    e2e_times = time_steps(e2e_step, None, e2e_steps, dstream)
+    barrier()
+    e2e_ms = max_over_ranks(sum(e2e_times)) / e2e_steps
+    h2d = sum_over_ranks(float(xh.numel() * 2 + gh.numel() * 2 + uh.numel() * 2))
+    d2h = sum_over_ranks(float(yh.numel() * 2))
+    e2e = {"value": total_flops / (e2e_ms * 1e-3) / 1e12, "unit": UNIT, "h2d_bytes_per_step": int(h2d),
+           "d2h_bytes_per_step": int(d2h), "ms_per_step": e2e_ms,
+           "path": "llk_swiglu C ABI, pinned host X/Wg/Wu/Y, copies in the timed region"}
+    # Packed weights (PackedWeights + L4-cache role): weights resident,
+    # X in / Y out per step.
+    pw = llk.PackedWeights(gd, ud)
+
+    def e2e_packed_step():
+        pw(xh, out=yh)
+
+    for _ in range(2):
+        e2e_packed_step()
+    p_times = time_steps(e2e_packed_step, None, e2e_steps, dstream)
+    p_ms = max_over_ranks(sum(p_times)) / e2e_steps
+    e2e_packed = {"value": total_flops / (p_ms * 1e-3) / 1e12, "unit": UNIT,
+                  "h2d_bytes_per_step": int(sum_over_ranks(float(xh.numel() * 2))),
+                  "d2h_bytes_per_step": int(d2h), "ms_per_step": p_ms}
+    pw.close()
+
+    extras = {}
+    cpu = None
+    if world == 1 and not args.quick:
+        extras = single_gpu_extras(args, dev, stream, flush, peak_tf, peak_gbs)
+        if not args.no_cpu_baseline:
+            cpu = cpu_baseline(x, wg, wu)
+
+    clocks = sampler.summary() if sampler else None
+    if rank == 0:
+        line = {
+            "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": job_ms, "higher_is_better": True, "scaling": "strong",
+            "vs_baseline": None, "dtype": "bf16",
+            "data": "synthetic (seeded splitmix64/Box-Muller, X~N(0,1), W~N(0,0.02), rounded to bf16)",
+            "config": {"workload": "c3 llama7b-prefill swiglu", "M": M, "K": K, "N": N,
+                       "parallelism": f"N-column-sharded x{world} (no collective)" if world > 1 else "single GPU",
+                       "shard_cols_rank0": n_r, "l2": "flushed before every timed step (256 MiB write)",
+                       "timing": "CUDA events around each kernel launch, summed, max over ranks"},
+            "roofline": {"bound": "tensor", "achieved": achieved, "peak": peak_tf, "unit": "TFLOP/s",
+                         "frac": achieved / peak_tf, "traffic": traffic,
+                         "peak_source": f"{peak_src} bf16 burst (MEASURED_PEAKS.json)",
+                         "kernel": "tc_swiglu_kernel<TC_SWIGLU_BF16>",
+                         "algorithmic_work": "4*M*N_rank*K FLOP per launch"},
+            "e2e": e2e, "e2e_packed_weights": e2e_packed,
+            "gpu_launches": args.steps,
+            "clocks": clocks,
+            "wall_s_timed_region": t_wall,
+        }
+        if cpu:
+            line["cpu_baseline"] = cpu
+        line.update(extras)
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.barrier(device_ids=[local])
+        dist.destroy_process_group()
+    return 0
+
+
+def single_gpu_extras(args, dev, stream, flush, peak_tf, peak_gbs):
+    """Secondary measurements on one GPU: the micro.mma matmul (config 2)
+    and the decode shapes (config 4) -- same timing rules."""
+    import torch
+
+    import dslcompiler_b200 as llk
+    from dslcompiler_b200 import datagen as dg
+
+    out = {}
+    steps = max(5, min(args.steps, 200))
+    a, b = dg.config_inputs("c2")
+    ad, bd = bf16_tensor(a).to(dev), bf16_tensor(b).to(dev)
+    cd = torch.empty((4096, 4096), dtype=torch.float32, device=dev)
+    fn = lambda: llk.matmul(ad, bd, cd)  # noqa: E731
+    for _ in range(3):
+        fn()
+    t = time_steps(fn, flush, steps, stream)
+    ms = sum(t) / len(t)
+    out["matmul_c2"] = {"tflops": 2.0 * 4096 ** 3 / (ms * 1e-3) / 1e12, "ms": ms,
+                        "frac_of_peak": 2.0 * 4096 ** 3 / (ms * 1e-3) / 1e12 / peak_tf}
+    del ad, bd, cd
+    dec = {}
+    for cfg in ("c4_m1", "c4_m4", "c4_m16"):
+        c = dg.CONFIGS[cfg]
+        x, wg, wu = dg.config_inputs(cfg)
+        xd, gd, ud = bf16_tensor(x).to(dev), bf16_tensor(wg).to(dev), bf16_tensor(wu).to(dev)
+        yd = torch.empty((c["M"], c["N"]), dtype=torch.bfloat16, device=dev)
+        fn = lambda: llk.fused_swiglu(xd, gd, ud, out=yd)  # noqa: E731
+        for _ in range(3):
+            fn()
+        t = time_steps(fn, flush, steps, stream)
+        ms = sum(t) / len(t)
+        byts = 2 * c["M"] * c["K"] + 4 * c["K"] * c["N"] + 2 * c["M"] * c["N"]
+        dec[cfg] = {"us": ms * 1e3, "GB/s": byts / (ms * 1e-3) / 1e9, "frac_of_hbm": byts / (ms * 1e-3) / 1e9 / peak_gbs,
+                    "tflops": 4.0 * c["M"] * c["N"] * c["K"] / (ms * 1e-3) / 1e12}
+        del xd, gd, ud, yd
+    out["decode_c4"] = dec
+    torch.cuda.synchronize()
+    llk.synchronize(dev.index)
+    return out
+
+
+def main(argv=None):
+    ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=2000)
+    ap.add_argument("--warmup", type=int, default=50)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--quick", action="store_true", help="skip the single-GPU extras and the CPU baseline")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args(argv)
+    if args.warmup < 3:
+        args.warmup = 3
+    rank, _, world = dist_env()
+    if world != args.gpus and rank == 0:
+        print(f"warning: --gpus {args.gpus} but WORLD_SIZE={world}", file=sys.stderr)
+    if args.impl == "reference":
+        return reference_arm(args)
+    return our_arm(args)
+
+
+if __name__ == "__main__":
+    sys.exit(main())

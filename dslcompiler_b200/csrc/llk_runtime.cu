@@ -36,7 +36,9 @@ thread_local int g_last_status = LLK_OK;
 struct DeviceBuffer {
   void *ptr = nullptr;
   size_t bytes = 0;
-  cudaError_t ensure(size_t need) {
+  // Grows the buffer to at least `need` bytes; a new buffer is zero-filled
+  // when `zero` is set.
+  cudaError_t ensure(size_t need, bool zero = false) {
     if (need <= bytes) return cudaSuccess;
     if (ptr) cudaFree(ptr);
     ptr = nullptr;
@@ -44,6 +46,7 @@ struct DeviceBuffer {
     size_t alloc = need + need / 8;
     cudaError_t e = cudaMalloc(&ptr, alloc);
     if (e == cudaSuccess) bytes = alloc;
+    if (e == cudaSuccess && zero) e = cudaMemset(ptr, 0, alloc);
     return e;
   }
 };
@@ -281,19 +284,24 @@ int launch_device(DeviceState &ds, int op, const DevTensor &x, const DevTensor &
   if (variant == LLK_VARIANT_DECODE) {
     const size_t need = decode_workspace_bytes(M, N, K, ds.sm_count);
     void *ws = scratch;
-    if (need > 0 && (ws == nullptr || scratch_bytes < need)) {
-      if (scratch != nullptr) return LLK_ERR_NOMEM;
+    if (ws != nullptr) {
+      // Caller scratch: its tile counters start from an unknown state.
+      if (scratch_bytes < need) return LLK_ERR_NOMEM;
+      const size_t off = decode_counter_offset(M, N);
+      if (cudaMemsetAsync(static_cast<char *>(ws) + off, 0, need - off, stream) != cudaSuccess) return LLK_ERR_CUDA;
+    } else {
       std::lock_guard<std::mutex> lk(ds.mu);
-      if (ds.workspace.ensure(need) != cudaSuccess) return LLK_ERR_NOMEM;
+      if (ds.workspace.ensure(need, true) != cudaSuccess) return LLK_ERR_NOMEM;
       ws = ds.workspace.ptr;
     }
-    CUtensorMap tg, tu;
-    int rc;
     const DecodePlan d = decode_plan(M, N, K, ds.sm_count);
-    if ((rc = encode_tmap(&tg, wg.data, N, K, wg.ld * 2, 64, d.block_k)) != LLK_OK) return rc;
-    if ((rc = encode_tmap(&tu, wu.data, N, K, wu.ld * 2, 64, d.block_k)) != LLK_OK) return rc;
-    e = decode_launch(tg, tu, x.data, x.ld, const_cast<void *>(y.data), y.ld, y_f32, M, N, K, ws, ds.status,
-                      ds.sm_count, stream);
+    CUtensorMap tg, tu, tx;
+    int rc;
+    if ((rc = encode_tmap(&tg, wg.data, N, K, wg.ld * 2, 64, 64)) != LLK_OK) return rc;
+    if ((rc = encode_tmap(&tu, wu.data, N, K, wu.ld * 2, 64, 64)) != LLK_OK) return rc;
+    if ((rc = encode_tmap(&tx, x.data, K, M, x.ld * 2, 64, d.block_m)) != LLK_OK) return rc;
+    e = decode_launch(tg, tu, tx, const_cast<void *>(y.data), y.ld, y_f32, M, N, K, ws, ds.status, ds.sm_count,
+                      stream);
     return e == cudaSuccess ? LLK_OK : LLK_ERR_CUDA;
   }
 
@@ -384,6 +392,8 @@ int read_and_clear_status(DeviceState &ds, cudaStream_t stream) {
   if (cudaStreamSynchronize(stream) != cudaSuccess) return LLK_ERR_CUDA;
   if (v != 0) {
     cudaMemsetAsync(ds.status, 0, sizeof(int), stream);
+    // A kernel that gave up may have left decode tile counters non-zero.
+    if (ds.workspace.ptr) cudaMemsetAsync(ds.workspace.ptr, 0, ds.workspace.bytes, stream);
     cudaStreamSynchronize(stream);
     return LLK_ERR_TIMEOUT;
   }
@@ -508,6 +518,19 @@ int llk_synchronize(int device, void *stream) {
   DeviceState *ds;
   if ((rc = device_init(dev, &ds)) != LLK_OK) return rc;
   return read_and_clear_status(*ds, static_cast<cudaStream_t>(stream));
+}
+
+int llk_diag_timeout_probe(int device, int64_t limit_ns) {
+  if (limit_ns <= 0) return LLK_ERR_ARG;
+  llk_gpu_context g;
+  std::memset(&g, 0, sizeof(g));
+  g.device = device;
+  int dev, rc;
+  if ((rc = resolve_device(&g, &dev)) != LLK_OK) return rc;
+  DeviceState *ds;
+  if ((rc = device_init(dev, &ds)) != LLK_OK) return rc;
+  if (diag_timeout_launch(ds->status, static_cast<uint64_t>(limit_ns), nullptr) != cudaSuccess) return LLK_ERR_CUDA;
+  return read_and_clear_status(*ds, nullptr);
 }
 
 // ---------------------------------------------------------- packed weights

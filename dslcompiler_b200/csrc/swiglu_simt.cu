@@ -82,3 +82,32 @@ cudaError_t simt_launch(int mode, const void *x, int64_t ldx, int64_t sxk, const
 }
 
 }  // namespace llk_b200
+
+// ------------------------------------------------------------------ diag
+// A kernel that waits on an mbarrier nothing will ever arrive at, with the
+// same bounded wait the production kernels use.  The wait gives up after
+// `limit_ns`, records LLK_ERR_TIMEOUT in the device status word and the
+// kernel returns normally, leaving the context usable.  It exists so the
+// timeout path can be exercised on a GPU without faulting or hanging it.
+namespace llk_b200 {
+namespace {
+__global__ void diag_timeout_kernel(int *status, uint64_t limit_ns) {
+  __shared__ __align__(8) uint64_t bar;
+  __shared__ int abort;
+  if (threadIdx.x == 0) {
+    mbar_init(&bar, 1);
+    abort = 0;
+    fence_mbar_init();
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    if (!mbar_wait_bounded(&bar, 0, &abort, LLK_ERR_TIMEOUT, limit_ns)) atomicExch(status, abort);
+  }
+}
+}  // namespace
+
+cudaError_t diag_timeout_launch(int *status, uint64_t limit_ns, cudaStream_t stream) {
+  diag_timeout_kernel<<<1, 32, 0, stream>>>(status, limit_ns);
+  return cudaGetLastError();
+}
+}  // namespace llk_b200

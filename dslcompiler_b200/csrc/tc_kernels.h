@@ -38,4 +38,7 @@ cudaError_t simt_launch(int mode, const void *x, int64_t ldx, int64_t sxk, const
                         int64_t ldw, int64_t swn, int64_t ldwu, int64_t swun, void *y, int64_t ldy, int64_t syn,
                         int y_f32, int64_t M, int64_t N, int64_t K, cudaStream_t stream);
 
+// Diagnostic: a bounded wait that is made to expire (see swiglu_simt.cu).
+cudaError_t diag_timeout_launch(int *status, uint64_t limit_ns, cudaStream_t stream);
+
 }  // namespace llk_b200

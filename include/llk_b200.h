@@ -134,6 +134,14 @@ const char *llk_status_string(int status);
  * LLK_OK; clears the device's error word. */
 int llk_synchronize(int device, void *stream);
 
+/* Diagnostic: launches a kernel whose bounded device-side wait is made to
+ * expire after `limit_ns` (nothing ever arrives on its barrier), waits for
+ * it and returns the device status -- LLK_ERR_TIMEOUT when the timeout path
+ * works.  No counterpart in the reference (its waits are unbounded,
+ * runtime/ThreadPool.cpp:96-103); it lets the failure path be tested on a
+ * GPU without a fault or a hang. */
+int llk_diag_timeout_probe(int device, int64_t limit_ns);
+
 /* ---- packed weights (runtime/PackedWeights.cpp:5-37, PackedWeights.h:13-49,
  *      and the L4 weight cache of include/LLK/Runtime/JitCache.h:143-146) --- */
 

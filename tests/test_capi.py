@@ -1,0 +1,147 @@
+"""The C-ABI library: it loads, exports every symbol include/llk_b200.h
+declares, and its host-side logic (argument checks, shard assignment,
+kernel keys, plan cache, status strings) behaves -- without a GPU."""
+import ctypes
+import os
+import re
+
+import numpy as np
+import pytest
+
+import dslcompiler_b200 as llk
+from dslcompiler_b200 import capi, build
+from tests.conftest import ROOT
+
+HEADER = os.path.join(ROOT, "include", "llk_b200.h")
+
+
+def declared_symbols():
+    src = open(HEADER).read()
+    src = re.sub(r"/\*.*?\*/", "", src, flags=re.S)
+    return sorted(set(re.findall(r"\b(llk_[a-z0-9_]+)\s*\(", src)))
+
+
+def test_library_builds_and_loads():
+    build.build()
+    assert os.path.exists(capi.LIB_PATH)
+    assert capi.lib() is not None
+
+
+def test_every_declared_symbol_is_exported():
+    L = ctypes.CDLL(capi.LIB_PATH)
+    syms = declared_symbols()
+    assert len(syms) >= 20
+    missing = [s for s in syms if not hasattr(L, s)]
+    assert not missing, missing
+    # and the Python binding covers all of them
+    assert set(syms) <= set(capi.PROTOTYPES), set(syms) - set(capi.PROTOTYPES)
+
+
+def test_struct_layouts_match_reference():
+    # JitCache.h:30-62 layouts: Tensor2D 40 B, MemRef2D 56 B, KernelContext 16 B
+    assert ctypes.sizeof(capi.Tensor2D) == 40
+    assert ctypes.sizeof(capi.MemRef2D) == 56
+    assert ctypes.sizeof(capi.KernelContext) == 16
+
+
+@pytest.mark.parametrize("M,bucket", [(1, 0), (3, 1), (8, 2), (32, 3), (128, 4), (2048, 4)])
+def test_classify_m(M, bucket):
+    assert llk.classify_m(M) == bucket
+
+
+def test_shard_columns_even_and_uneven():
+    # 11008 = 86 tiles of 128 -> 11,11,11,11,11,11,10,10 at 8 shards
+    widths = []
+    prev = 0
+    for i in range(8):
+        b, e = llk.shard_columns(11008, 8, i)
+        assert b == prev
+        prev = e
+        widths.append(e - b)
+    assert prev == 11008
+    assert [w // 128 for w in widths] == [11, 11, 11, 11, 11, 11, 10, 10]
+    # 28672 = 224 tiles -> 28 each
+    assert {llk.shard_columns(28672, 8, i)[1] - llk.shard_columns(28672, 8, i)[0] for i in range(8)} == {3584}
+    # ragged N, more shards than tiles
+    spans = [llk.shard_columns(130, 4, i) for i in range(4)]
+    assert spans[0] == (0, 128) and spans[1] == (128, 130) and spans[2] == (130, 130) and spans[3] == (130, 130)
+    with pytest.raises(llk.LLKError):
+        llk.shard_columns(100, 0, 0)
+    with pytest.raises(llk.LLKError):
+        llk.shard_columns(100, 2, 2)
+
+
+def test_kernel_key_hash_deterministic_and_field_sensitive():
+    a = llk.KernelKey(N=11008, K=4096, M_bucket=4)
+    b = llk.KernelKey(N=11008, K=4096, M_bucket=4)
+    c = llk.KernelKey(N=11008, K=4096, M_bucket=3)
+    assert a.hash() == b.hash() != c.hash()
+
+
+def test_plan_cache_lru_and_stats():
+    llk.cache_clear()
+    llk.cache_set_max_entries(2)
+    try:
+        p = llk.KernelKey(N=11008, K=4096, M_bucket=4).plan(2048)
+        assert p["variant"] == capi.VARIANTS["tc"] and p["block_m"] == 128 and p["block_n"] == 128
+        assert p["grid"] >= 1 and p["smem_bytes"] > 100 * 1024
+        llk.KernelKey(N=11008, K=4096, M_bucket=4).plan(2048)
+        s = llk.cache_stats()
+        assert s["hits"] == 1 and s["misses"] == 1 and s["size"] == 1
+        for n in (128, 256, 384):
+            llk.KernelKey(N=n, K=64).plan(128)
+        s = llk.cache_stats()
+        assert s["size"] == 2 and s["evictions"] == 2
+    finally:
+        llk.cache_set_max_entries(1024)
+        llk.cache_clear()
+
+
+def test_shape_errors_reported_before_device_use():
+    # LLKOps.cpp:42-83 rules: M/K/N mismatches are LLK_ERR_SHAPE even with no GPU
+    x = np.zeros((4, 8), np.uint16)
+    wg = np.zeros((7, 16), np.uint16)
+    wu = np.zeros((8, 16), np.uint16)
+    with pytest.raises(llk.LLKError) as e:
+        llk.fused_swiglu(x, wg, wu)
+    assert e.value.status == capi.LLK_ERR_SHAPE
+    with pytest.raises(llk.LLKError) as e:
+        llk.fused_swiglu(x, wu, np.zeros((8, 15), np.uint16))
+    assert e.value.status == capi.LLK_ERR_SHAPE
+    y = np.zeros((4, 16), np.uint16)
+    st = llk.swiglu_c_abi(x, wu, wu, np.zeros((5, 16), np.uint16))
+    assert st == capi.LLK_ERR_SHAPE
+    with pytest.raises(TypeError):
+        llk.fused_swiglu(x.astype(np.float32), wu, wu)
+    del y
+
+
+def test_no_cpu_fallback_without_gpu():
+    try:
+        import torch
+        has_gpu = torch.cuda.is_available()
+    except Exception:
+        has_gpu = False
+    if has_gpu:
+        pytest.skip("a GPU is present")
+    x = np.zeros((4, 8), np.uint16)
+    w = np.zeros((8, 16), np.uint16)
+    with pytest.raises(llk.LLKError) as e:
+        llk.fused_swiglu(x, w, w)
+    assert e.value.status == capi.LLK_ERR_DEVICE
+    with pytest.raises(llk.LLKError) as e:
+        llk.probe(0)
+    assert e.value.status == capi.LLK_ERR_DEVICE
+
+
+def test_status_strings():
+    for s in range(10):
+        assert capi.status_string(s) != "unknown status"
+    assert capi.status_string(99) == "unknown status"
+
+
+def test_memref_shim_reports_status():
+    L = capi.lib()
+    m = capi.MemRef2D()
+    L.llk_swiglu_memref(None, ctypes.byref(m), ctypes.byref(m), None, ctypes.byref(m))
+    assert L.llk_last_status() == capi.LLK_ERR_ARG
