@@ -104,6 +104,7 @@ PROTOTYPES = {
     "llk_cuda_probe": (_i, [_i, _P(CudaTarget)]),
     "llk_kernel_key_hash": (_u64, [_P(KernelKeyC)]),
     "llk_plan_lookup": (_i, [_P(KernelKeyC), _i64, _P(LaunchPlan)]),
+    "llk_plan_insert": (_i, [_P(KernelKeyC), _P(LaunchPlan)]),
     "llk_cache_stats": (None, [_P(_u64), _P(_u64), _P(_u64)]),
     "llk_cache_set_max_entries": (None, [_u64]),
     "llk_cache_clear": (None, []),

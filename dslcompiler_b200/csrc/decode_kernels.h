@@ -20,13 +20,17 @@ bool decode_supported(int64_t M, int64_t N, int64_t K, int y_f32);
 DecodePlan decode_plan(int64_t M, int64_t N, int64_t K, int sm_count);
 // Device workspace the launch needs (split-K partial sums + tile counters).
 size_t decode_workspace_bytes(int64_t M, int64_t N, int64_t K, int sm_count);
-// Byte offset of the per-tile counters inside the workspace; they must be
-// zero before the first launch (each launch leaves them zero again).
+// Byte offset and size of the per-tile counters inside the workspace; they
+// must be zero before the first launch (each launch leaves them zero again).
 size_t decode_counter_offset(int64_t M, int64_t N);
-// wg, wu: weight tensor maps, box {64 columns, 64 k}; x: token tensor map,
-// box {64 k, block_m rows of decode_plan}.
+size_t decode_counter_bytes(int64_t N);
+// Whether a plan (possibly a tuned override) is launchable for this shape.
+bool decode_plan_valid(int64_t M, int64_t N, int64_t K, const DecodePlan &d);
+// wg, wu: weight tensor maps with a 64-column x 64-k box (2-D over
+// row-major [K, N], or 3-D over slab-major packed weights when slab_major);
+// x: token tensor map, box {64 k, d.block_m rows}.
 cudaError_t decode_launch(const CUtensorMap &wg, const CUtensorMap &wu, const CUtensorMap &x, void *y, int64_t ldy,
-                          int y_f32, int64_t M, int64_t N, int64_t K, void *workspace, int *status, int sm_count,
-                          cudaStream_t stream);
+                          int y_f32, int64_t M, int64_t N, int64_t K, void *workspace, int *status,
+                          const DecodePlan &d, int slab_major, cudaStream_t stream);
 
 }  // namespace llk_b200

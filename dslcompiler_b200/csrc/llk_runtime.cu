@@ -134,6 +134,20 @@ int encode_tmap(CUtensorMap *m, const void *base, uint64_t inner, uint64_t outer
   return r == CUDA_SUCCESS ? LLK_OK : LLK_ERR_ALIGN;
 }
 
+// Slab-major packed weights ([N/64][K][64] bf16, see llk_pack_weights) as a
+// 3-D tensor map {64, K, N/64} with a {64, 64, 1} box: every box is one
+// contiguous 8 KB block.
+int encode_tmap_slabs(CUtensorMap *m, const void *base, uint64_t K, uint64_t n_slabs) {
+  cuuint64_t dims[3] = {64, K, n_slabs};
+  cuuint64_t strides[2] = {128, K * 128};
+  cuuint32_t box[3] = {64, 64, 1};
+  cuuint32_t estr[3] = {1, 1, 1};
+  CUresult r = g_encode(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void *>(base), dims, strides, box, estr,
+                        CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                        CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS ? LLK_OK : LLK_ERR_ALIGN;
+}
+
 bool aligned16(const void *p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
 // ------------------------------------------------------------- plan cache
@@ -251,9 +265,18 @@ llk_launch_plan plan_for(const llk_kernel_key &key, int64_t M, int sm_count) {
 struct DevTensor {
   const void *data;
   int64_t rows, cols, ld, inner;  // ld = row stride, inner = column stride (elements)
+  int slab_major = 0;             // weights only: slab-major packed layout
 };
 
+// TMA map for a weight operand: 2-D over row-major [K, N] or 3-D over the
+// slab-major packed layout.
+int encode_weight_tmap(CUtensorMap *m, const DevTensor &w) {
+  if (w.slab_major) return encode_tmap_slabs(m, w.data, static_cast<uint64_t>(w.rows), (w.cols + 63) / 64);
+  return encode_tmap(m, w.data, w.cols, w.rows, w.ld * 2, 64, 64);
+}
+
 // Y = SwiGLU(X, Wg, Wu) or C (+)= A B on device tensors.  op: LLK_OP_*.
+// Called with ds.mu held (it guards the staging buffers and the workspace).
 int launch_device(DeviceState &ds, int op, const DevTensor &x, const DevTensor &wg, const DevTensor &wu,
                   const DevTensor &y, int y_f32, int accumulate, int requested, void *scratch, size_t scratch_bytes,
                   cudaStream_t stream) {
@@ -261,15 +284,18 @@ int launch_device(DeviceState &ds, int op, const DevTensor &x, const DevTensor &
   if (M == 0 || N == 0) return LLK_OK;
   if (M > INT32_MAX || N > INT32_MAX || K > INT32_MAX) return LLK_ERR_SHAPE;
   const bool swiglu = (op == LLK_OP_FUSED_SWIGLU);
-  const bool unit = x.inner == 1 && wg.inner == 1 && (!swiglu || wu.inner == 1) && y.inner == 1;
-  const bool tma_ok = unit && aligned16(x.data) && aligned16(wg.data) && (!swiglu || aligned16(wu.data)) &&
-                      (x.ld * 2) % 16 == 0 && (wg.ld * 2) % 16 == 0 && (!swiglu || (wu.ld * 2) % 16 == 0) &&
-                      x.ld >= K && wg.ld >= N && (!swiglu || wu.ld >= N);
+  const bool slab = wg.slab_major != 0;
+  auto weight_ok = [&](const DevTensor &w) {
+    return w.slab_major || (w.inner == 1 && aligned16(w.data) && (w.ld * 2) % 16 == 0 && w.ld >= N);
+  };
+  const bool tma_ok = x.inner == 1 && y.inner == 1 && aligned16(x.data) && (x.ld * 2) % 16 == 0 && x.ld >= K &&
+                      weight_ok(wg) && (!swiglu || weight_ok(wu));
   const bool decode_ok = swiglu && tma_ok && decode_supported(M, N, K, y_f32);
   const int variant = choose_variant(requested, tma_ok, decode_ok, M, K);
   if (variant < 0) return LLK_ERR_UNSUPPORTED;
 
   llk_kernel_key key = make_key(op, y_f32 ? LLK_DTYPE_FP32 : LLK_DTYPE_BF16, M, N, K, variant);
+  key.weight_layout = slab ? 1 : 0;  // Layout::PackedKN analogue
   llk_launch_plan plan = plan_for(key, M, ds.sm_count);
   cudaError_t e = cudaSuccess;
 
@@ -277,7 +303,7 @@ int launch_device(DeviceState &ds, int op, const DevTensor &x, const DevTensor &
     int mode = swiglu ? 0 : (accumulate ? 2 : 1);
     e = simt_launch(mode, x.data, x.ld, x.inner, wg.data, swiglu ? wu.data : wg.data, wg.ld, wg.inner,
                     swiglu ? wu.ld : wg.ld, swiglu ? wu.inner : wg.inner, const_cast<void *>(y.data), y.ld, y.inner,
-                    y_f32, M, N, K, stream);
+                    y_f32, M, N, K, slab ? 1 : 0, stream);
     return e == cudaSuccess ? LLK_OK : LLK_ERR_CUDA;
   }
 
@@ -288,19 +314,22 @@ int launch_device(DeviceState &ds, int op, const DevTensor &x, const DevTensor &
       // Caller scratch: its tile counters start from an unknown state.
       if (scratch_bytes < need) return LLK_ERR_NOMEM;
       const size_t off = decode_counter_offset(M, N);
-      if (cudaMemsetAsync(static_cast<char *>(ws) + off, 0, need - off, stream) != cudaSuccess) return LLK_ERR_CUDA;
+      if (cudaMemsetAsync(static_cast<char *>(ws) + off, 0, decode_counter_bytes(N), stream) != cudaSuccess)
+        return LLK_ERR_CUDA;
     } else {
-      std::lock_guard<std::mutex> lk(ds.mu);
+      // ds.mu is held by the caller (run_op) for the whole launch.
       if (ds.workspace.ensure(need, true) != cudaSuccess) return LLK_ERR_NOMEM;
       ws = ds.workspace.ptr;
     }
-    const DecodePlan d = decode_plan(M, N, K, ds.sm_count);
+    DecodePlan d = {plan.block_m, plan.block_n, plan.block_k, plan.stages, plan.split_k, plan.grid, plan.threads,
+                     plan.smem_bytes};
+    if (!decode_plan_valid(M, N, K, d)) d = decode_plan(M, N, K, ds.sm_count);
     CUtensorMap tg, tu, tx;
     int rc;
-    if ((rc = encode_tmap(&tg, wg.data, N, K, wg.ld * 2, 64, 64)) != LLK_OK) return rc;
-    if ((rc = encode_tmap(&tu, wu.data, N, K, wu.ld * 2, 64, 64)) != LLK_OK) return rc;
+    if ((rc = encode_weight_tmap(&tg, wg)) != LLK_OK) return rc;
+    if ((rc = encode_weight_tmap(&tu, wu)) != LLK_OK) return rc;
     if ((rc = encode_tmap(&tx, x.data, K, M, x.ld * 2, 64, d.block_m)) != LLK_OK) return rc;
-    e = decode_launch(tg, tu, tx, const_cast<void *>(y.data), y.ld, y_f32, M, N, K, ws, ds.status, ds.sm_count,
+    e = decode_launch(tg, tu, tx, const_cast<void *>(y.data), y.ld, y_f32, M, N, K, ws, ds.status, d, slab ? 1 : 0,
                       stream);
     return e == cudaSuccess ? LLK_OK : LLK_ERR_CUDA;
   }
@@ -309,9 +338,9 @@ int launch_device(DeviceState &ds, int op, const DevTensor &x, const DevTensor &
   CUtensorMap ta, tb0, tb1;
   int rc;
   if ((rc = encode_tmap(&ta, x.data, K, M, x.ld * 2, 64, 128)) != LLK_OK) return rc;
-  if ((rc = encode_tmap(&tb0, wg.data, N, K, wg.ld * 2, 64, 64)) != LLK_OK) return rc;
+  if ((rc = encode_weight_tmap(&tb0, wg)) != LLK_OK) return rc;
   if (swiglu) {
-    if ((rc = encode_tmap(&tb1, wu.data, N, K, wu.ld * 2, 64, 64)) != LLK_OK) return rc;
+    if ((rc = encode_weight_tmap(&tb1, wu)) != LLK_OK) return rc;
   } else {
     tb1 = tb0;
   }
@@ -333,8 +362,9 @@ int launch_device(DeviceState &ds, int op, const DevTensor &x, const DevTensor &
   p.status = ds.status;
   p.b_lbo = 64 * 64 * 2;  // 8 KB between 64-column slabs
   p.b_sbo = 8 * 128;      // 1 KB between 8-row k groups
-  const int grid = p.num_tiles < ds.sm_count ? p.num_tiles : ds.sm_count;
-  (void)plan;
+  p.slab_major = slab ? 1 : 0;
+  int grid = p.num_tiles < ds.sm_count ? p.num_tiles : ds.sm_count;
+  if (plan.variant == LLK_VARIANT_TC && plan.grid >= 1 && plan.grid <= grid) grid = plan.grid;
   e = tc_launch(mode, ta, tb0, tb1, p, grid, stream);
   return e == cudaSuccess ? LLK_OK : LLK_ERR_CUDA;
 }
@@ -402,7 +432,8 @@ int read_and_clear_status(DeviceState &ds, cudaStream_t stream) {
 
 // Common body of the SwiGLU / matmul entry points.  wu may equal wg (matmul).
 int run_op(int op, const Tensor2D *x, const Tensor2D *wg, const Tensor2D *wu, Tensor2D *y, int y_f32, int accumulate,
-           KernelContext *ctx, const llk_gpu_context *gpu) {
+           KernelContext *ctx, const llk_gpu_context *gpu, const DevTensor *packed_g = nullptr,
+           const DevTensor *packed_u = nullptr) {
   if (gpu && (gpu->y_dtype != LLK_DTYPE_BF16 && gpu->y_dtype != LLK_DTYPE_FP32)) return LLK_ERR_ARG;
   if (gpu && (gpu->variant < LLK_VARIANT_AUTO || gpu->variant > LLK_VARIANT_SIMT)) return LLK_ERR_ARG;
   int dev, rc;
@@ -418,8 +449,12 @@ int run_op(int op, const Tensor2D *x, const Tensor2D *wg, const Tensor2D *wu, Te
   {
     std::lock_guard<std::mutex> lk(ds->mu);
     if ((rc = stage_in(x, 2, ds->stage[0], true, stream, &sx)) != LLK_OK) return rc;
-    if ((rc = stage_in(wg, 2, ds->stage[1], true, stream, &sg)) != LLK_OK) return rc;
-    if (wu != wg) {
+    if (packed_g) {
+      sg.t = *packed_g;
+      su.t = *packed_u;
+    } else if ((rc = stage_in(wg, 2, ds->stage[1], true, stream, &sg)) != LLK_OK) {
+      return rc;
+    } else if (wu != wg) {
       if ((rc = stage_in(wu, 2, ds->stage[2], true, stream, &su)) != LLK_OK) return rc;
     } else {
       su = sg;
@@ -534,22 +569,36 @@ int llk_diag_timeout_probe(int device, int64_t limit_ns) {
 }
 
 // ---------------------------------------------------------- packed weights
+// Layout: each matrix is stored slab-major, [ceil(N/64)][K][64] bf16 -- the
+// 64-column slabs the kernels load as one TMA box each, so every box is a
+// contiguous 8 KB block instead of 64 rows of 128 bytes strided by the row
+// pitch.  This is runtime/PackedWeights.cpp's k-block packing turned
+// around: there K is blocked and rows stay N wide (the CPU kernel walks n in
+// the inner loop); here N is blocked at the TMA box width and K runs inside
+// a block (the tensor cores consume [64 k x 64 n] tiles).  Columns past N in
+// the last slab are zero.
 struct llk_packed_weights {
   int device;
-  int64_t K, N;
-  void *wg;  // device, row-major [K, N], pitch N (padded to a multiple of 8)
+  int64_t K, N, n_slabs;
+  void *wg;  // device, slab-major
   void *wu;
-  int64_t ld;
   int64_t bytes;
 };
 
-static int copy_weight(void *dst, int64_t ld, const Tensor2D *w, cudaStream_t stream) {
-  if (w->stride1 != 1) return LLK_ERR_ALIGN;
+static int copy_weight_slabs(void *dst, int64_t K, int64_t N, const Tensor2D *w, cudaStream_t stream) {
+  if (w->stride1 != 1 || w->stride0 < w->dim1) return LLK_ERR_ALIGN;
   const bool dev = is_device_ptr(w->data);
-  cudaError_t e = cudaMemcpy2DAsync(dst, static_cast<size_t>(ld) * 2, w->data, static_cast<size_t>(w->stride0) * 2,
-                                    static_cast<size_t>(w->dim1) * 2, static_cast<size_t>(w->dim0),
-                                    dev ? cudaMemcpyDeviceToDevice : cudaMemcpyHostToDevice, stream);
-  return e == cudaSuccess ? LLK_OK : LLK_ERR_CUDA;
+  const int64_t n_slabs = (N + 63) / 64;
+  for (int64_t s = 0; s < n_slabs; ++s) {
+    const int64_t cols = (N - 64 * s) < 64 ? (N - 64 * s) : 64;
+    cudaError_t e = cudaMemcpy2DAsync(static_cast<char *>(dst) + s * K * 128, 128,
+                                      static_cast<const char *>(w->data) + s * 64 * 2,
+                                      static_cast<size_t>(w->stride0) * 2, static_cast<size_t>(cols) * 2,
+                                      static_cast<size_t>(K), dev ? cudaMemcpyDeviceToDevice : cudaMemcpyHostToDevice,
+                                      stream);
+    if (e != cudaSuccess) return LLK_ERR_CUDA;
+  }
+  return LLK_OK;
 }
 
 int llk_repack(llk_packed_weights *pw, const Tensor2D *wg, const Tensor2D *wu, const llk_gpu_context *gpu) {
@@ -559,8 +608,8 @@ int llk_repack(llk_packed_weights *pw, const Tensor2D *wg, const Tensor2D *wu, c
   cudaStream_t stream = gpu ? static_cast<cudaStream_t>(gpu->stream) : nullptr;
   if (pw->K == 0 || pw->N == 0) return LLK_OK;
   int rc;
-  if ((rc = copy_weight(pw->wg, pw->ld, wg, stream)) != LLK_OK) return rc;
-  if ((rc = copy_weight(pw->wu, pw->ld, wu, stream)) != LLK_OK) return rc;
+  if ((rc = copy_weight_slabs(pw->wg, pw->K, pw->N, wg, stream)) != LLK_OK) return rc;
+  if ((rc = copy_weight_slabs(pw->wu, pw->K, pw->N, wu, stream)) != LLK_OK) return rc;
   return cudaStreamSynchronize(stream) == cudaSuccess ? LLK_OK : LLK_ERR_CUDA;
 }
 
@@ -576,8 +625,8 @@ int llk_pack_weights(const Tensor2D *wg, const Tensor2D *wu, const llk_gpu_conte
   pw->device = dev;
   pw->K = wg->dim0;
   pw->N = wg->dim1;
-  pw->ld = (pw->N + 7) / 8 * 8;  // 16-byte row pitch for TMA
-  const size_t bytes = static_cast<size_t>(pw->K) * pw->ld * 2;
+  pw->n_slabs = (pw->N + 63) / 64;
+  const size_t bytes = static_cast<size_t>(pw->K) * pw->n_slabs * 128;
   pw->bytes = static_cast<int64_t>(2 * bytes);
   pw->wg = pw->wu = nullptr;
   if (bytes > 0) {
@@ -620,8 +669,7 @@ int llk_packed_weights_info(const llk_packed_weights *pw, int64_t *K, int64_t *N
 int llk_swiglu_packed(const Tensor2D *x, const llk_packed_weights *pw, Tensor2D *y, KernelContext *ctx,
                       const llk_gpu_context *gpu) {
   if (!x || !pw || !y) return LLK_ERR_ARG;
-  Tensor2D wg = {pw->wg, pw->K, pw->N, pw->ld, 1};
-  Tensor2D wu = {pw->wu, pw->K, pw->N, pw->ld, 1};
+  if (x->dim1 != pw->K || y->dim0 != x->dim0 || y->dim1 != pw->N || x->dim0 < 0) return LLK_ERR_SHAPE;
   llk_gpu_context g;
   if (gpu) {
     g = *gpu;
@@ -631,7 +679,19 @@ int llk_swiglu_packed(const Tensor2D *x, const llk_packed_weights *pw, Tensor2D 
   }
   if (g.device >= 0 && g.device != pw->device) return LLK_ERR_ARG;
   g.device = pw->device;
-  return llk_swiglu_ex(x, &wg, &wu, y, ctx, &g);
+  if (g.y_dtype != LLK_DTYPE_BF16 && g.y_dtype != LLK_DTYPE_FP32) return LLK_ERR_ARG;
+  DevTensor pg, pu;
+  pg.data = pw->wg;
+  pu.data = pw->wu;
+  pg.rows = pu.rows = pw->K;
+  pg.cols = pu.cols = pw->N;
+  pg.ld = pu.ld = 64;
+  pg.inner = pu.inner = 1;
+  pg.slab_major = pu.slab_major = 1;
+  Tensor2D wview = {pw->wg, pw->K, pw->N, pw->N, 1};  // shape carrier for the argument checks
+  int rc = check_swiglu(x, &wview, &wview, y);
+  if (rc != LLK_OK) return rc;
+  return run_op(LLK_OP_FUSED_SWIGLU, x, &wview, &wview, y, g.y_dtype == LLK_DTYPE_FP32 ? 1 : 0, 0, ctx, &g, &pg, &pu);
 }
 
 // ---------------------------------------------------------------- sharding
@@ -703,6 +763,28 @@ int llk_plan_lookup(const llk_kernel_key *key, int64_t M, llk_launch_plan *out) 
     cudaGetLastError();
   }
   *out = plan_for(*key, M, sm);
+  return LLK_OK;
+}
+
+int llk_plan_insert(const llk_kernel_key *key, const llk_launch_plan *plan) {
+  if (!key || !plan) return LLK_ERR_ARG;
+  if (plan->variant < LLK_VARIANT_TC || plan->variant > LLK_VARIANT_SIMT || plan->variant != key->thread_count)
+    return LLK_ERR_ARG;
+  const std::string kb = key_bytes(*key);
+  std::lock_guard<std::mutex> lk(g_cache.mu);
+  auto it = g_cache.index.find(kb);
+  if (it != g_cache.index.end()) {
+    it->second->plan = *plan;
+    g_cache.lru.splice(g_cache.lru.begin(), g_cache.lru, it->second);
+    return LLK_OK;
+  }
+  g_cache.lru.push_front({kb, *plan});
+  g_cache.index[kb] = g_cache.lru.begin();
+  while (g_cache.lru.size() > g_cache.max_entries) {
+    g_cache.index.erase(g_cache.lru.back().key);
+    g_cache.lru.pop_back();
+    ++g_cache.evictions;
+  }
   return LLK_OK;
 }
 

@@ -92,6 +92,28 @@ __device__ __forceinline__ void tma_load_2d(void *smem_dst, const CUtensorMap *m
       : "memory");
 }
 
+// 3-D tiled load (c0 innermost).  Used for slab-major packed weights.
+__device__ __forceinline__ void tma_load_3d(void *smem_dst, const CUtensorMap *map, uint64_t *bar, int32_t c0,
+                                            int32_t c1, int32_t c2) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4, %5}], "
+      "[%2];" ::"r"(smem_u32(smem_dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_u32(bar)), "r"(c0), "r"(c1), "r"(c2)
+      : "memory");
+}
+
+// Loads the 64-column x 64-k weight slab whose first column is n (a
+// multiple of 64) and first row k: from a row-major [K, N] tensor map
+// (2-D, {N, K}) or from slab-major packed weights (3-D, {64, K, N/64}).
+__device__ __forceinline__ void tma_load_weight_slab(void *smem_dst, const CUtensorMap *map, uint64_t *bar, int n,
+                                                     int k, bool slab_major) {
+  if (slab_major) {
+    tma_load_3d(smem_dst, map, bar, 0, k, n >> 6);
+  } else {
+    tma_load_2d(smem_dst, map, bar, n, k);
+  }
+}
+
 // --------------------------------------------------------------- tcgen05
 // Shared-memory matrix descriptor (tcgen05 format): start address >> 4 in
 // bits 0-13, leading-dimension byte offset >> 4 in 16-29, stride-dimension

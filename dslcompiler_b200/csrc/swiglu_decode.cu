@@ -40,6 +40,10 @@ constexpr uint32_t kSlab = 64 * kBK * 2;  // 64 n x 64 k bf16 = 8 KB
 constexpr int kMaxSlots = 4;       // contributors per tile the workspace holds
 constexpr uint64_t kWaitLimitNs = 2000000000ull;
 constexpr int kSmemBudget = 220 * 1024;
+// The per-tile counters sit at the start of the workspace, at the same place
+// for every shape, so a workspace reused across shapes never has a counter
+// landing on another call's partial sums.  256 KB = 65536 tiles (N <= 8 M).
+constexpr size_t kCounterRegion = 256 * 1024;
 
 struct DecodeParams {
   int M, N, K;
@@ -49,7 +53,7 @@ struct DecodeParams {
   long long total;   // n_tiles * kb_per_tile work units
   int stages;
   int y_f32;
-  const uint16_t *x;  // only for documentation; X is read through its tensor map
+  int slab_major;    // weight tensor maps describe slab-major packed weights
   void *y;
   long long ldy;
   float *partials;   // [n_tiles][kMaxSlots][2][Mp][128] f32
@@ -151,10 +155,10 @@ __global__ void __launch_bounds__(kThreads, 1)
         uint8_t *s = smem + stage * stage_bytes;
         mbar_arrive_expect_tx(&st->full[stage], 4 * kSlab + x_bytes);
         const int n0 = t * kTileN, k0 = kb * kBK;
-        tma_load_2d(s + 0 * kSlab, &tm_wg, &st->full[stage], n0, k0);
-        tma_load_2d(s + 1 * kSlab, &tm_wg, &st->full[stage], n0 + 64, k0);
-        tma_load_2d(s + 2 * kSlab, &tm_wu, &st->full[stage], n0, k0);
-        tma_load_2d(s + 3 * kSlab, &tm_wu, &st->full[stage], n0 + 64, k0);
+        tma_load_weight_slab(s + 0 * kSlab, &tm_wg, &st->full[stage], n0, k0, p.slab_major);
+        tma_load_weight_slab(s + 1 * kSlab, &tm_wg, &st->full[stage], n0 + 64, k0, p.slab_major);
+        tma_load_weight_slab(s + 2 * kSlab, &tm_wu, &st->full[stage], n0, k0, p.slab_major);
+        tma_load_weight_slab(s + 3 * kSlab, &tm_wu, &st->full[stage], n0 + 64, k0, p.slab_major);
         tma_load_2d(s + 4 * kSlab, &tm_x, &st->full[stage], k0, 0);
         ++issued;
         if (++stage == static_cast<uint32_t>(p.stages)) {
@@ -286,15 +290,34 @@ __global__ void __launch_bounds__(kThreads, 1)
       epi_bar();
       if (st->is_last) {
         __threadfence();
-        if (n < p.N) {
-          for (int m = 0; m < p.M; ++m) {
-            float gs = 0.f, us = 0.f;
-            for (int s = 0; s < n_contrib; ++s) {
-              const float *ps = tile_ws + (size_t)s * 2 * p.Mp * kTileN;
-              gs += __ldcg(ps + (size_t)m * kTileN + r);
-              us += __ldcg(ps + (size_t)(p.Mp + m) * kTileN + r);
+        // Sum the contributors' slots in slot order (deterministic), 16
+        // token rows at a time so the loads of a row block are in flight
+        // together.
+        for (int m0 = 0; m0 < p.M; m0 += 16) {
+          float gs[16], us[16];
+#pragma unroll
+          for (int j = 0; j < 16; ++j) gs[j] = us[j] = 0.f;
+#pragma unroll
+          for (int sl = 0; sl < kMaxSlots; ++sl) {
+            if (sl < n_contrib) {
+              const float *ps = tile_ws + (size_t)sl * 2 * p.Mp * kTileN + (size_t)m0 * kTileN + r;
+              float gv[16], uv[16];
+#pragma unroll
+              for (int j = 0; j < 16; ++j) {
+                gv[j] = __ldcg(ps + (size_t)j * kTileN);
+                uv[j] = __ldcg(ps + (size_t)(p.Mp + j) * kTileN);
+              }
+#pragma unroll
+              for (int j = 0; j < 16; ++j) {
+                gs[j] += gv[j];
+                us[j] += uv[j];
+              }
             }
-            store_y(p, m, n, silu_mul(gs, us));
+          }
+          if (n < p.N) {
+#pragma unroll
+            for (int j = 0; j < 16; ++j)
+              if (m0 + j < p.M) store_y(p, m0 + j, n, silu_mul(gs[j], us[j]));
           }
         }
         if (etid == 0) p.counters[t] = 0;
@@ -322,10 +345,13 @@ int stage_bytes_for(int Mp) { return 4 * static_cast<int>(kSlab) + ((Mp * kBK * 
 
 }  // namespace
 
-int decode_max_m() { return 64; }
+// Above 16 tokens the tcgen05 prefill kernel streams the weights as fast
+// (measured on B200 for N = 14336, K = 4096) and needs no workspace.
+int decode_max_m() { return 16; }
 
 bool decode_supported(int64_t M, int64_t N, int64_t K, int) {
-  return M >= 1 && M <= 128 && N >= 1 && K >= 1 && N <= INT32_MAX && K <= INT32_MAX;
+  return M >= 1 && M <= 128 && N >= 1 && K >= 1 && N <= INT32_MAX && K <= INT32_MAX &&
+         static_cast<size_t>((N + kTileN - 1) / kTileN) * sizeof(int) <= kCounterRegion;
 }
 
 DecodePlan decode_plan(int64_t M, int64_t N, int64_t K, int sm_count) {
@@ -343,7 +369,7 @@ DecodePlan decode_plan(int64_t M, int64_t N, int64_t K, int sm_count) {
   // and no tile may be split over more CTAs than the workspace has slots
   const long long kb_per_tile = (K + kBK - 1) / kBK;
   const long long min_units = (kb_per_tile + kMaxSlots - 2) / (kMaxSlots - 1);
-  if (total / grid < min_units) grid = (total + min_units - 1) / min_units;
+  if (total / grid < min_units) grid = total / min_units;
   if (grid < 1) grid = 1;
   d.grid = static_cast<int>(grid);
   d.split_k = static_cast<int>((grid + ((N + kTileN - 1) / kTileN) - 1) / ((N + kTileN - 1) / kTileN));
@@ -355,19 +381,29 @@ DecodePlan decode_plan(int64_t M, int64_t N, int64_t K, int sm_count) {
 size_t decode_workspace_bytes(int64_t M, int64_t N, int64_t, int) {
   const int Mp = padded_m(M);
   const size_t n_tiles = static_cast<size_t>((N + kTileN - 1) / kTileN);
-  return n_tiles * kMaxSlots * 2 * Mp * kTileN * sizeof(float) + n_tiles * sizeof(int);
+  return kCounterRegion + n_tiles * kMaxSlots * 2 * Mp * kTileN * sizeof(float);
 }
 
-size_t decode_counter_offset(int64_t M, int64_t N) {
-  const int Mp = padded_m(M);
-  const size_t n_tiles = static_cast<size_t>((N + kTileN - 1) / kTileN);
-  return n_tiles * kMaxSlots * 2 * Mp * kTileN * sizeof(float);
+size_t decode_counter_offset(int64_t, int64_t) { return 0; }
+size_t decode_counter_bytes(int64_t N) { return static_cast<size_t>((N + kTileN - 1) / kTileN) * sizeof(int); }
+
+bool decode_plan_valid(int64_t M, int64_t N, int64_t K, const DecodePlan &d) {
+  if (d.block_m != padded_m(M) || d.block_n != kTileN || d.block_k != kBK) return false;
+  if (d.stages < 2 || d.stages > 8 || d.grid < 1) return false;
+  const int sb = stage_bytes_for(d.block_m);
+  if (d.stages * sb + static_cast<int>(sizeof(DecodeTail)) + 1024 > 227 * 1024) return false;
+  const long long kb_per_tile = (K + kBK - 1) / kBK;
+  const long long total = ((N + kTileN - 1) / kTileN) * kb_per_tile;
+  if (d.grid > total) return false;
+  // no tile may have more contributors than the workspace has slots
+  const long long min_units = (kb_per_tile + kMaxSlots - 2) / (kMaxSlots - 1);
+  return total / d.grid >= min_units;
 }
 
 cudaError_t decode_launch(const CUtensorMap &wg, const CUtensorMap &wu, const CUtensorMap &x, void *y, int64_t ldy,
-                          int y_f32, int64_t M, int64_t N, int64_t K, void *workspace, int *status, int sm_count,
-                          cudaStream_t stream) {
-  const DecodePlan d = decode_plan(M, N, K, sm_count);
+                          int y_f32, int64_t M, int64_t N, int64_t K, void *workspace, int *status,
+                          const DecodePlan &d, int slab_major, cudaStream_t stream) {
+  if (!decode_plan_valid(M, N, K, d)) return cudaErrorInvalidValue;
   DecodeParams p;
   p.M = static_cast<int>(M);
   p.N = static_cast<int>(N);
@@ -378,15 +414,16 @@ cudaError_t decode_launch(const CUtensorMap &wg, const CUtensorMap &wu, const CU
   p.total = static_cast<long long>(p.n_tiles) * p.kb_per_tile;
   p.stages = d.stages;
   p.y_f32 = y_f32;
-  p.x = nullptr;
+  p.slab_major = slab_major;
   p.y = y;
   p.ldy = ldy;
-  p.partials = static_cast<float *>(workspace);
-  p.counters = reinterpret_cast<int *>(static_cast<char *>(workspace) + decode_counter_offset(M, N));
+  p.counters = static_cast<int *>(workspace);
+  p.partials = reinterpret_cast<float *>(static_cast<char *>(workspace) + kCounterRegion);
   p.status = status;
-  cudaError_t e = cudaFuncSetAttribute(decode_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, d.smem_bytes);
+  const int smem = d.stages * stage_bytes_for(d.block_m) + static_cast<int>(sizeof(DecodeTail)) + 1024;
+  cudaError_t e = cudaFuncSetAttribute(decode_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
   if (e != cudaSuccess) return e;
-  decode_kernel<<<d.grid, kThreads, d.smem_bytes, stream>>>(wg, wu, x, p);
+  decode_kernel<<<d.grid, kThreads, smem, stream>>>(wg, wu, x, p);
   return cudaGetLastError();
 }
 

@@ -26,15 +26,25 @@ __global__ void __launch_bounds__(256) simt_kernel(const uint16_t *__restrict__ 
                                                    const uint16_t *__restrict__ wg, int64_t ldw, int64_t swn,
                                                    const uint16_t *__restrict__ wu, int64_t ldwu, int64_t swun,
                                                    void *y, int64_t ldy, int64_t syn, int y_f32, int64_t M,
-                                                   int64_t N, int64_t K) {
+                                                   int64_t N, int64_t K, int slab_major) {
   const int64_t n = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
   const int64_t m = blockIdx.y;
   if (n >= N || m >= M) return;
+  // Element (k, n) of a weight: row-major with strides, or slab-major
+  // packed ([n / 64][k][n % 64]).
+  int64_t wbase = 0, wk = ldw, wbase_u = 0, wk_u = ldwu;
+  if (slab_major) {
+    wbase = wbase_u = (n >> 6) * K * 64 + (n & 63);
+    wk = wk_u = 64;
+  } else {
+    wbase = n * swn;
+    wbase_u = n * swun;
+  }
   float g = 0.0f, u = 0.0f;
   for (int64_t k = 0; k < K; ++k) {
     const float xv = bf16_at(x, m * ldx + k * sxk);
-    g = fmaf(xv, bf16_at(wg, k * ldw + n * swn), g);
-    if (MODE == 0) u = fmaf(xv, bf16_at(wu, k * ldwu + n * swun), u);
+    g = fmaf(xv, bf16_at(wg, wbase + k * wk), g);
+    if (MODE == 0) u = fmaf(xv, bf16_at(wu, wbase_u + k * wk_u), u);
   }
   float r;
   if (MODE == 0) {
@@ -56,7 +66,7 @@ __global__ void __launch_bounds__(256) simt_kernel(const uint16_t *__restrict__ 
 
 cudaError_t simt_launch(int mode, const void *x, int64_t ldx, int64_t sxk, const void *wg, const void *wu,
                         int64_t ldw, int64_t swn, int64_t ldwu, int64_t swun, void *y, int64_t ldy, int64_t syn,
-                        int y_f32, int64_t M, int64_t N, int64_t K, cudaStream_t stream) {
+                        int y_f32, int64_t M, int64_t N, int64_t K, int slab_major, cudaStream_t stream) {
   if (M <= 0 || N <= 0) return cudaSuccess;
   if (M > 65535) return cudaErrorInvalidValue;
   dim3 block(256);
@@ -67,13 +77,15 @@ cudaError_t simt_launch(int mode, const void *x, int64_t ldx, int64_t sxk, const
   switch (mode) {
     case 0:
       simt_kernel<0><<<grid, block, 0, stream>>>(xp, ldx, sxk, gp, ldw, swn, up, ldwu, swun, y, ldy, syn, y_f32, M, N,
-                                                 K);
+                                                 K, slab_major);
       break;
     case 1:
-      simt_kernel<1><<<grid, block, 0, stream>>>(xp, ldx, sxk, gp, ldw, swn, gp, ldw, swn, y, ldy, syn, 1, M, N, K);
+      simt_kernel<1><<<grid, block, 0, stream>>>(xp, ldx, sxk, gp, ldw, swn, gp, ldw, swn, y, ldy, syn, 1, M, N, K,
+                                                 slab_major);
       break;
     case 2:
-      simt_kernel<2><<<grid, block, 0, stream>>>(xp, ldx, sxk, gp, ldw, swn, gp, ldw, swn, y, ldy, syn, 1, M, N, K);
+      simt_kernel<2><<<grid, block, 0, stream>>>(xp, ldx, sxk, gp, ldw, swn, gp, ldw, swn, y, ldy, syn, 1, M, N, K,
+                                                 slab_major);
       break;
     default:
       return cudaErrorInvalidValue;

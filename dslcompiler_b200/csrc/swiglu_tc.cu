@@ -119,13 +119,14 @@ __global__ void __launch_bounds__(kThreads, 1)
           const int k0 = kb * kBK;
           tma_load_2d(sa, &tm_a, &st->full[stage], k0, m0);
           if (kSwiglu) {
-            tma_load_2d(sb + 0 * kSlabBytes, &tm_b0, &st->full[stage], n0, k0);
-            tma_load_2d(sb + 1 * kSlabBytes, &tm_b0, &st->full[stage], n0 + 64, k0);
-            tma_load_2d(sb + 2 * kSlabBytes, &tm_b1, &st->full[stage], n0, k0);
-            tma_load_2d(sb + 3 * kSlabBytes, &tm_b1, &st->full[stage], n0 + 64, k0);
+            tma_load_weight_slab(sb + 0 * kSlabBytes, &tm_b0, &st->full[stage], n0, k0, p.slab_major);
+            tma_load_weight_slab(sb + 1 * kSlabBytes, &tm_b0, &st->full[stage], n0 + 64, k0, p.slab_major);
+            tma_load_weight_slab(sb + 2 * kSlabBytes, &tm_b1, &st->full[stage], n0, k0, p.slab_major);
+            tma_load_weight_slab(sb + 3 * kSlabBytes, &tm_b1, &st->full[stage], n0 + 64, k0, p.slab_major);
           } else {
 #pragma unroll
-            for (int j = 0; j < 4; ++j) tma_load_2d(sb + j * kSlabBytes, &tm_b0, &st->full[stage], n0 + 64 * j, k0);
+            for (int j = 0; j < 4; ++j)
+              tma_load_weight_slab(sb + j * kSlabBytes, &tm_b0, &st->full[stage], n0 + 64 * j, k0, p.slab_major);
           }
           ++issued;
           if (++stage == kStages) {

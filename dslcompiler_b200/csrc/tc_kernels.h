@@ -23,6 +23,7 @@ struct TcParams {
   int *status;        // device-visible error word (LLK_ERR_TIMEOUT on a wait that gave up)
   uint32_t b_lbo;     // MN-major B descriptor: bytes between 64-column slabs
   uint32_t b_sbo;     // MN-major B descriptor: bytes between 8-row k groups
+  int slab_major;     // B tensor maps describe slab-major packed weights (3-D)
 };
 
 int tc_smem_bytes();
@@ -33,10 +34,11 @@ cudaError_t tc_launch(int mode, const CUtensorMap &a, const CUtensorMap &b0, con
 
 // CUDA-core kernel for any strides / alignment (small or odd shapes).
 // x, wg, wu bf16; y bf16 (y_f32 == 0) or f32.  mode 0 = swiglu, 1 = matmul,
-// 2 = matmul accumulating into y.
+// 2 = matmul accumulating into y.  slab_major: wg/wu are slab-major packed
+// weights ([N/64][K][64]; ld/stride arguments ignored).
 cudaError_t simt_launch(int mode, const void *x, int64_t ldx, int64_t sxk, const void *wg, const void *wu,
                         int64_t ldw, int64_t swn, int64_t ldwu, int64_t swun, void *y, int64_t ldy, int64_t syn,
-                        int y_f32, int64_t M, int64_t N, int64_t K, cudaStream_t stream);
+                        int y_f32, int64_t M, int64_t N, int64_t K, int slab_major, cudaStream_t stream);
 
 // Diagnostic: a bounded wait that is made to expire (see swiglu_simt.cu).
 cudaError_t diag_timeout_launch(int *status, uint64_t limit_ns, cudaStream_t stream);

@@ -228,6 +228,14 @@ class KernelKey:
         k = self.to_c()
         return lib().llk_kernel_key_hash(ctypes.byref(k))
 
+    def insert_plan(self, **plan) -> None:
+        """Install a launch plan for this key (a tuned schedule)."""
+        k = self.to_c()
+        p = capi.LaunchPlan()
+        for f, _ in capi.LaunchPlan._fields_:
+            setattr(p, f, int(plan.get(f, 0)))
+        check(lib().llk_plan_insert(ctypes.byref(k), ctypes.byref(p)), "llk_plan_insert")
+
     def plan(self, M: int) -> dict:
         k = self.to_c()
         p = capi.LaunchPlan()

@@ -221,6 +221,12 @@ typedef struct llk_launch_plan {
 
 uint64_t llk_kernel_key_hash(const llk_kernel_key *key);
 int llk_plan_lookup(const llk_kernel_key *key, int64_t M, llk_launch_plan *out);
+/* Installs a plan for a key (insertObjectCode, JitCache.h:116-119): a tuned
+ * schedule (llk-tune) overrides the built-in choice.  A plan the kernel
+ * cannot run for a call's shape is ignored at launch (the built-in plan is
+ * used).  key->thread_count carries the variant and must equal
+ * plan->variant. */
+int llk_plan_insert(const llk_kernel_key *key, const llk_launch_plan *plan);
 /* hits, misses, evictions of the plan cache. */
 void llk_cache_stats(uint64_t *hits, uint64_t *misses, uint64_t *evictions);
 void llk_cache_set_max_entries(uint64_t max_entries);

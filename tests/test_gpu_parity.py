@@ -329,3 +329,19 @@ def test_decode_caller_scratch():
     with pytest.raises(llk.LLKError) as e:
         llk.fused_swiglu(dev(x), dev(wg), dev(wu), variant="decode", scratch=small)
     assert e.value.status == capi.LLK_ERR_NOMEM
+
+
+@pytest.mark.parametrize("M,K,N", [(4, 1024, 200), (16, 4096, 14336), (300, 512, 136), (1, 64, 64)])
+@pytest.mark.parametrize("variant", ["auto", "tc", "decode", "simt"])
+def test_packed_slab_layout_matches_row_major(M, K, N, variant):
+    if variant == "decode" and M > 128:
+        pytest.skip("decode kernel serves M <= 128")
+    x, wg, wu = dg.swiglu_inputs(M, K, N, 1.0, 0.02, seed=N + M)
+    pw = llk.PackedWeights(dev(wg), dev(wu))  # packed from device buffers
+    assert pw.nbytes == 2 * K * ((N + 63) // 64) * 128
+    a = pw(dev(x), out_dtype="f32", variant=variant)
+    b = llk.fused_swiglu(dev(x), dev(wg), dev(wu), out_dtype="f32", variant=variant)
+    torch.cuda.synchronize()
+    llk.synchronize(0)
+    assert torch.equal(a, b)  # same kernel, same accumulation order: identical
+    pw.close()
