@@ -142,6 +142,46 @@ int llk_synchronize(int device, void *stream);
  * GPU without a fault or a hang. */
 int llk_diag_timeout_probe(int device, int64_t limit_ns);
 
+/* ---- decode without device allocation -------------------------------- */
+
+/* Size of the fixed device scratch array behind llk_swiglu_decode_noalloc
+ * (16 MiB; every GPU that loads the library holds it until exit). */
+#define LLK_DECODE_NOALLOC_SCRATCH_BYTES (16u << 20)
+
+/* The small-M (decode) fused SwiGLU for callers that cannot allocate device
+ * memory: code whose GPU memory is owned by another allocator (e.g. a
+ * framework's caching allocator that has reserved the HBM, where a raw
+ * cudaMalloc would fail or fragment it) or latency-critical loops where
+ * cudaMalloc/cudaFree would add host round trips and implicit device-wide
+ * synchronisation.  No counterpart in the reference (its CPU kernel takes
+ * scratch through KernelContext).
+ *
+ * It runs the same decode kernel as llk_swiglu_ex (variant DECODE), but its
+ * split-K workspace is a fixed file-scope device array of
+ * LLK_DECODE_NOALLOC_SCRATCH_BYTES, so the call allocates nothing: no
+ * cudaMalloc/cudaFree, no library allocator.  The caller passes inputs and
+ * outputs in DEVICE memory (host buffers are refused with LLK_ERR_ARG, as
+ * staging them would need device memory).  Limits: 1 <= M <= 128, and the
+ * workspace the shape needs, 262144 + ceil(N/128) * 4096 * Mp bytes (Mp = M
+ * rounded up to 16, 32, 64 or 128), must fit the array; larger shapes are
+ * refused with LLK_ERR_NOMEM.  Rows of X/Wg/Wu need 16-byte aligned starts
+ * and pitches (else LLK_ERR_ALIGN).  Y is bf16, or f32 when
+ * gpu->y_dtype == LLK_DTYPE_FP32.
+ *
+ * The first call on a device performs a one-time set-up with that device
+ * current (it looks up the array's device address with
+ * cudaGetSymbolAddress); make that first call before any stream capture.
+ * Every call shares the one array and it keeps the last call's contents:
+ * each call clears the counters that must start at zero.  Calls that overlap
+ * on the GPU (different streams, or threads without ordering) race on the
+ * array and corrupt each other's results -- serialise them.
+ *
+ * device_status, if not NULL, is a device int that receives LLK_ERR_TIMEOUT
+ * when a bounded wait in the kernel gives up (the call does not clear it).
+ * Asynchronous on gpu->stream (NULL gpu: current device, default stream). */
+int llk_swiglu_decode_noalloc(const Tensor2D *x, const Tensor2D *wg, const Tensor2D *wu, Tensor2D *y,
+                              int *device_status, const llk_gpu_context *gpu);
+
 /* ---- packed weights (runtime/PackedWeights.cpp:5-37, PackedWeights.h:13-49,
  *      and the L4 weight cache of include/LLK/Runtime/JitCache.h:143-146) --- */
 
