@@ -276,7 +276,7 @@ def our_arm(args):
     peak_tf, peak_gbs, peak_src = measured_peaks()
     my_ms = kernel_ms / args.steps
     achieved = 4.0 * M * n_r * K / (my_ms * 1e-3) / 1e12
-    traffic = profile_traffic("tc_swiglu_c3") if world == 1 else None
+    traffic = profile_traffic("tc2_swiglu_c3") if world == 1 else None
 
     # ----------------------------------------------------------- e2e
     # Through the reference-facing C ABI (llk_swiglu) with pinned host
@@ -340,7 +340,7 @@ def our_arm(args):
             "roofline": {"bound": "tensor", "achieved": achieved, "peak": peak_tf, "unit": "TFLOP/s",
                          "frac": achieved / peak_tf, "traffic": traffic,
                          "peak_source": f"{peak_src} bf16 burst (MEASURED_PEAKS.json)",
-                         "kernel": "tc_swiglu_kernel<TC_SWIGLU_BF16>",
+                         "kernel": "tc2_kernel<TC_SWIGLU_BF16> (CTA pairs)" if M > 128 else "tc_swiglu_kernel<TC_SWIGLU_BF16>",
                          "algorithmic_work": "4*M*N_rank*K FLOP per launch"},
             "e2e": e2e, "e2e_packed_weights": e2e_packed,
             "gpu_launches": args.steps,

@@ -204,15 +204,19 @@ llk_launch_plan build_plan(int variant, int op, int64_t M, int64_t N, int64_t K,
   p.variant = variant;
   if (variant == LLK_VARIANT_TC) {
     const int mode = (op == LLK_OP_MATMUL) ? TC_MATMUL_F32 : TC_SWIGLU_BF16;
-    p.block_m = 128;
+    // CTA pairs (256-row MMAs) once there are two row blocks; one CTA below.
+    const bool pair = M > 128;
+    p.block_m = pair ? 256 : 128;
     p.block_n = tc_tile_n(mode);
     p.block_k = 64;
-    p.stages = 4;
+    p.stages = pair ? 6 : 4;
     p.split_k = 1;
-    const int64_t tiles = ((M + 127) / 128) * ((N + p.block_n - 1) / p.block_n);
-    p.grid = static_cast<int>(tiles < sm_count ? tiles : sm_count);
+    const int64_t tiles = ((M + p.block_m - 1) / p.block_m) * ((N + p.block_n - 1) / p.block_n);
+    const int64_t ctas = pair ? 2 * tiles : tiles;
+    p.grid = static_cast<int>(ctas < sm_count ? ctas : sm_count);
+    if (pair) p.grid &= ~1;
     p.threads = tc_threads();
-    p.smem_bytes = tc_smem_bytes();
+    p.smem_bytes = pair ? tc2_smem_bytes() : tc_smem_bytes();
   } else if (variant == LLK_VARIANT_DECODE) {
     DecodePlan d = decode_plan(M, N, K, sm_count);
     p.block_m = d.block_m;
@@ -352,7 +356,10 @@ int launch_device(DeviceState &ds, int op, const DevTensor &x, const DevTensor &
   p.M = static_cast<int>(M);
   p.N = static_cast<int>(N);
   p.K = static_cast<int>(K);
-  p.m_tiles = static_cast<int>((M + 127) / 128);
+  // plan.block_m: 256 = CTA-pair kernel (swiglu_tc2.cu), 128 = one CTA per tile.
+  const bool pair = plan.variant == LLK_VARIANT_TC ? plan.block_m == 256 : M > 128;
+  const int rows = pair ? 256 : 128;
+  p.m_tiles = static_cast<int>((M + rows - 1) / rows);
   p.n_tiles = static_cast<int>((N + tile_n - 1) / tile_n);
   p.num_tiles = p.m_tiles * p.n_tiles;
   p.k_blocks = static_cast<int>((K + 63) / 64);
@@ -363,6 +370,11 @@ int launch_device(DeviceState &ds, int op, const DevTensor &x, const DevTensor &
   p.b_lbo = 64 * 64 * 2;  // 8 KB between 64-column slabs
   p.b_sbo = 8 * 128;      // 1 KB between 8-row k groups
   p.slab_major = slab ? 1 : 0;
+  if (pair) {
+    const int max_pairs = plan.variant == LLK_VARIANT_TC && plan.grid >= 2 ? plan.grid / 2 : 0;
+    e = tc2_launch(mode, ta, tb0, tb1, p, max_pairs, stream);
+    return e == cudaSuccess ? LLK_OK : LLK_ERR_CUDA;
+  }
   int grid = p.num_tiles < ds.sm_count ? p.num_tiles : ds.sm_count;
   if (plan.variant == LLK_VARIANT_TC && plan.grid >= 1 && plan.grid <= grid) grid = plan.grid;
   e = tc_launch(mode, ta, tb0, tb1, p, grid, stream);

@@ -1,0 +1,355 @@
+// swiglu_tc2.cu -- the prefill SwiGLU / micro.mma kernel on CTA PAIRS
+// (tcgen05 cta_group::2): one MMA instruction spans two SMs.
+//
+// Why: with one CTA issuing 128x256x16 MMAs, every MMA reads 4 KB of A and
+// 8 KB of B from that SM's shared memory while TMA fills the next stages;
+// the shared-memory operand path, not the tensor pipe, is the limiter (ncu:
+// ~80 % busy with the tensor pipe at ~71 %).  A pair issues 256x256x16 MMAs in
+// which each SM supplies 128 rows of A and HALF of B (128 columns), so the B
+// bytes each SM reads and loads per FLOP halve.
+//
+// Per pair and tile: Y rows [m0, m0+256) x 128 columns (SwiGLU: B = [Wg 128
+// columns from the leader CTA | Wu 128 columns from the peer CTA], so gate
+// lands in TMEM columns 0-127 and up in 128-255 of each CTA's accumulator),
+// or a 256 x 256 C tile (matmul: B columns n0.. from the leader, n0+128..
+// from the peer).
+//
+// Roles per CTA (6 warps), cluster = the pair:
+//   warp 0     TMA producer, both CTAs: own 128 rows of X and own B half into
+//              own shared memory; completion bytes go to the LEADER's full
+//              barrier (2-SM TMA form).  The leader alone posts the expected
+//              byte count of both CTAs.
+//   warp 1     TMEM owner in both CTAs (paired alloc); in the leader, the
+//              single MMA-issuing thread; its commits arrive on the stage /
+//              accumulator barriers of both CTAs.
+//   warps 2-5  epilogue in both CTAs on their own TMEM rows; each thread
+//              releases the accumulator by arriving on the leader's barrier.
+// All waits bounded; no TMA multicast (each CTA loads its own tiles).
+#include <cuda.h>
+#include <cuda_runtime.h>
+
+#include <cstdint>
+
+#include "sm100_ptx.cuh"
+#include "tc_kernels.h"
+
+namespace llk_b200 {
+
+namespace {
+
+constexpr int kThreads = 192;
+constexpr int kStages = 6;
+constexpr int kRows = 128;                          // rows of X per CTA
+constexpr int kBK = 64;
+constexpr int kMmaN = 256;
+constexpr uint32_t kABytes = kRows * kBK * 2;       // 16 KB
+constexpr uint32_t kSlabBytes = 64 * kBK * 2;       // 8 KB
+constexpr uint32_t kBBytes = 2 * kSlabBytes;        // 16 KB: this CTA's 128 columns
+constexpr uint32_t kStageBytes = kABytes + kBBytes;  // 32 KB
+constexpr uint32_t kTmemCols = 512;
+constexpr uint64_t kWaitLimitNs = 2000000000ull;
+
+struct __align__(8) PairTail {
+  uint64_t full[kStages];   // leader's copy is the one used
+  uint64_t empty[kStages];  // both CTAs
+  uint64_t tmem_full[2];    // both CTAs
+  uint64_t tmem_empty[2];   // leader's copy is the one used (256 arrivals)
+  uint64_t mma_done;
+  uint32_t tmem_base;
+  int abort;
+};
+
+template <int MODE>
+__global__ void __launch_bounds__(kThreads, 1)
+    tc2_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__ CUtensorMap tm_b0,
+               const __grid_constant__ CUtensorMap tm_b1, const TcParams p) {
+  constexpr bool kSwiglu = (MODE == TC_SWIGLU_BF16 || MODE == TC_SWIGLU_F32);
+  constexpr int kTileN = kSwiglu ? 128 : 256;
+
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  PairTail *st = reinterpret_cast<PairTail *>(smem + kStages * kStageBytes);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const uint32_t rank = cluster_ctarank();  // 0 = leader, 1 = peer
+  const int pair = blockIdx.x >> 1;
+  const int n_pairs = gridDim.x >> 1;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kStages; ++s) {
+      mbar_init(&st->full[s], 1);
+      mbar_init(&st->empty[s], 1);
+    }
+    for (int a = 0; a < 2; ++a) {
+      mbar_init(&st->tmem_full[a], 1);
+      mbar_init(&st->tmem_empty[a], 256);
+    }
+    mbar_init(&st->mma_done, 1);
+    st->abort = 0;
+    fence_mbar_init();
+  }
+  if (warp == 0 && lane == 0) {
+    tma_prefetch_desc(&tm_a);
+    tma_prefetch_desc(&tm_b0);
+    if (kSwiglu) tma_prefetch_desc(&tm_b1);
+  }
+  if (warp == 1) {
+    tmem_alloc_pair(&st->tmem_base, kTmemCols);
+    tmem_relinquish_pair();
+  }
+  tc_fence_before();
+  __syncthreads();
+  cluster_sync_all();  // the peer may only signal the leader's barriers once they exist
+  tc_fence_after();
+  const uint32_t tmem_base = st->tmem_base;
+  volatile int *abort = &st->abort;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      const uint32_t leader_full = map_shared_rank(smem_u32(&st->full[0]), 0);
+      uint32_t stage = 0, phase = 0, issued = 0;
+      bool ok = true;
+      for (int tile = pair; tile < p.num_tiles && ok; tile += n_pairs) {
+        const int m0 = (tile % p.m_tiles) * (2 * kRows) + static_cast<int>(rank) * kRows;
+        const int n0 = (tile / p.m_tiles) * kTileN;
+        for (int kb = 0; kb < p.k_blocks; ++kb) {
+          if (!mbar_wait_bounded(&st->empty[stage], phase ^ 1u, abort, LLK_ERR_TIMEOUT, kWaitLimitNs)) {
+            ok = false;
+            break;
+          }
+          uint8_t *sa = smem + stage * kStageBytes;
+          uint8_t *sb = sa + kABytes;
+          const uint32_t bar = leader_full + stage * 8u;
+          if (rank == 0) mbar_arrive_expect_tx(&st->full[stage], 2 * kStageBytes);
+          const int k0 = kb * kBK;
+          tma_load_2d_pair(sa, &tm_a, bar, k0, m0);
+          if (kSwiglu) {
+            const CUtensorMap *w = rank == 0 ? &tm_b0 : &tm_b1;
+            tma_load_weight_slab_pair(sb, w, bar, n0, k0, p.slab_major);
+            tma_load_weight_slab_pair(sb + kSlabBytes, w, bar, n0 + 64, k0, p.slab_major);
+          } else {
+            const int nb = n0 + static_cast<int>(rank) * 128;
+            tma_load_weight_slab_pair(sb, &tm_b0, bar, nb, k0, p.slab_major);
+            tma_load_weight_slab_pair(sb + kSlabBytes, &tm_b0, bar, nb + 64, k0, p.slab_major);
+          }
+          ++issued;
+          if (++stage == kStages) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+      }
+      if (!ok && rank == 0) {
+        // Loads in flight land on the leader's barriers: wait (bounded) for them.
+        const uint32_t n = issued < kStages ? issued : kStages;
+        for (uint32_t i = 0; i < n; ++i) {
+          const uint32_t idx = issued - 1 - i;
+          int dummy = 0;
+          mbar_wait_bounded(&st->full[idx % kStages], (idx / kStages) & 1u, &dummy, 1, 100000000ull);
+        }
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0 && rank == 0) {
+      const uint32_t idesc = make_idesc_bf16_f32(2 * kRows, kMmaN, false, true);
+      const uint32_t smem_base = smem_u32(smem);
+      uint32_t stage = 0, phase = 0;
+      bool ok = true;
+      int local = 0;
+      for (int tile = pair; tile < p.num_tiles && ok; tile += n_pairs, ++local) {
+        const uint32_t acc = local & 1;
+        if (!mbar_wait_bounded(&st->tmem_empty[acc], ((local >> 1) & 1) ^ 1u, abort, LLK_ERR_TIMEOUT,
+                               kWaitLimitNs)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + acc * kMmaN;
+        for (int kb = 0; kb < p.k_blocks; ++kb) {
+          if (!mbar_wait_bounded(&st->full[stage], phase, abort, LLK_ERR_TIMEOUT, kWaitLimitNs)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t a_addr = smem_base + stage * kStageBytes;
+          const uint32_t b_addr = a_addr + kABytes;
+#pragma unroll
+          for (int kk = 0; kk < kBK / 16; ++kk) {
+            const uint64_t a_desc = make_smem_desc_sw128(a_addr + kk * 32, 16, 1024);
+            const uint64_t b_desc = make_smem_desc_sw128(b_addr + kk * 2048, kSlabBytes, 1024);
+            tc_mma_bf16_pair(d_tmem, a_desc, b_desc, idesc, (kb > 0 || kk > 0) ? 1u : 0u);
+          }
+          tc_commit_pair_mc(&st->empty[stage], 0x3);
+          if (++stage == kStages) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+        if (!ok) break;
+        tc_commit_pair_mc(&st->tmem_full[acc], 0x3);
+      }
+      tc_commit_pair_mc(&st->mma_done, 0x1);
+      int dummy = 0;
+      mbar_wait_bounded(&st->mma_done, 0, &dummy, 1, 100000000ull);
+    }
+    __syncwarp();
+  } else {
+    // ------------------------------------------------------------ epilogue
+    const int q = warp & 3;
+    const int row_in_tile = q * 32 + lane;
+    const uint32_t leader_tmem_empty = map_shared_rank(smem_u32(&st->tmem_empty[0]), 0);
+    int local = 0;
+    for (int tile = pair; tile < p.num_tiles; tile += n_pairs, ++local) {
+      const uint32_t acc = local & 1;
+      if (!mbar_wait_bounded(&st->tmem_full[acc], (local >> 1) & 1, abort, LLK_ERR_TIMEOUT, kWaitLimitNs)) break;
+      tc_fence_after();
+      const int m0 = (tile % p.m_tiles) * (2 * kRows) + static_cast<int>(rank) * kRows;
+      const int n0 = (tile / p.m_tiles) * kTileN;
+      const int row = m0 + row_in_tile;
+      const uint32_t t_row = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + acc * kMmaN;
+      if (kSwiglu) {
+#pragma unroll 1
+        for (int c = 0; c < 128; c += 32) {
+          uint32_t g[32], u[32];
+          tmem_ld_32x32b_x32(t_row + c, g);
+          tmem_ld_32x32b_x32(t_row + 128 + c, u);
+          tmem_ld_wait();
+          const int col = n0 + c;
+          if (row < p.M && col < p.N) {
+            float y[32];
+#pragma unroll
+            for (int j = 0; j < 32; ++j) y[j] = silu_mul(__uint_as_float(g[j]), __uint_as_float(u[j]));
+            if (MODE == TC_SWIGLU_BF16) {
+              uint16_t *dst = reinterpret_cast<uint16_t *>(p.y) + (int64_t)row * p.ldy + col;
+              if (p.vec_ok && col + 32 <= p.N) {
+                uint4 *d4 = reinterpret_cast<uint4 *>(dst);
+#pragma unroll
+                for (int v = 0; v < 4; ++v)
+                  d4[v] = make_uint4(pack_bf16x2(y[8 * v + 0], y[8 * v + 1]), pack_bf16x2(y[8 * v + 2], y[8 * v + 3]),
+                                     pack_bf16x2(y[8 * v + 4], y[8 * v + 5]), pack_bf16x2(y[8 * v + 6], y[8 * v + 7]));
+              } else {
+#pragma unroll
+                for (int j = 0; j < 32; ++j)
+                  if (col + j < p.N) dst[j] = static_cast<uint16_t>(pack_bf16x2(y[j], 0.f));
+              }
+            } else {
+              float *dst = reinterpret_cast<float *>(p.y) + (int64_t)row * p.ldy + col;
+              if (p.vec_ok && col + 32 <= p.N) {
+                float4 *d4 = reinterpret_cast<float4 *>(dst);
+#pragma unroll
+                for (int v = 0; v < 8; ++v) d4[v] = make_float4(y[4 * v], y[4 * v + 1], y[4 * v + 2], y[4 * v + 3]);
+              } else {
+#pragma unroll
+                for (int j = 0; j < 32; ++j)
+                  if (col + j < p.N) dst[j] = y[j];
+              }
+            }
+          }
+        }
+      } else {
+#pragma unroll 1
+        for (int c = 0; c < 256; c += 32) {
+          uint32_t r[32];
+          tmem_ld_32x32b_x32(t_row + c, r);
+          tmem_ld_wait();
+          const int col = n0 + c;
+          if (row < p.M && col < p.N) {
+            float *dst = reinterpret_cast<float *>(p.y) + (int64_t)row * p.ldy + col;
+            if (p.vec_ok && col + 32 <= p.N) {
+              float4 *d4 = reinterpret_cast<float4 *>(dst);
+#pragma unroll
+              for (int v = 0; v < 8; ++v) {
+                float4 o = make_float4(__uint_as_float(r[4 * v]), __uint_as_float(r[4 * v + 1]),
+                                       __uint_as_float(r[4 * v + 2]), __uint_as_float(r[4 * v + 3]));
+                if (MODE == TC_MATMUL_F32_ACC) {
+                  const float4 c4 = d4[v];
+                  o.x += c4.x;
+                  o.y += c4.y;
+                  o.z += c4.z;
+                  o.w += c4.w;
+                }
+                d4[v] = o;
+              }
+            } else {
+#pragma unroll
+              for (int j = 0; j < 32; ++j) {
+                if (col + j < p.N) {
+                  float o = __uint_as_float(r[j]);
+                  if (MODE == TC_MATMUL_F32_ACC) o += dst[j];
+                  dst[j] = o;
+                }
+              }
+            }
+          }
+        }
+      }
+      tc_fence_before();
+      mbar_arrive_cluster(leader_tmem_empty + acc * 8u);
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  cluster_sync_all();  // no CTA leaves while its partner may still signal it
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc_pair(tmem_base, kTmemCols);
+  }
+  if (threadIdx.x == 0 && st->abort != 0 && p.status != nullptr) atomicExch(p.status, st->abort);
+}
+
+template <int MODE>
+cudaError_t launch_pair_mode(const CUtensorMap &a, const CUtensorMap &b0, const CUtensorMap &b1, const TcParams &p,
+                             int max_pairs, cudaStream_t stream) {
+  auto kern = tc2_kernel<MODE>;
+  const int smem = tc2_smem_bytes();
+  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+  if (e != cudaSuccess) return e;
+  cudaLaunchConfig_t cfg = {};
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 2;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.blockDim = dim3(kThreads);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  cfg.gridDim = dim3(2);
+  int clusters = 0;
+  e = cudaOccupancyMaxActiveClusters(&clusters, kern, &cfg);
+  if (e != cudaSuccess || clusters < 1) {
+    cudaGetLastError();
+    clusters = 1;
+  }
+  int pairs = p.num_tiles < clusters ? p.num_tiles : clusters;
+  if (max_pairs >= 1 && pairs > max_pairs) pairs = max_pairs;
+  cfg.gridDim = dim3(2 * pairs);
+  e = cudaLaunchKernelEx(&cfg, kern, a, b0, b1, p);
+  if (e != cudaSuccess) return e;
+  return cudaGetLastError();
+}
+
+}  // namespace
+
+int tc2_smem_bytes() { return kStages * kStageBytes + static_cast<int>(sizeof(PairTail)) + 1024; }
+
+cudaError_t tc2_launch(int mode, const CUtensorMap &a, const CUtensorMap &b0, const CUtensorMap &b1,
+                       const TcParams &p, int max_pairs, cudaStream_t stream) {
+  switch (mode) {
+    case TC_SWIGLU_BF16:
+      return launch_pair_mode<TC_SWIGLU_BF16>(a, b0, b1, p, max_pairs, stream);
+    case TC_SWIGLU_F32:
+      return launch_pair_mode<TC_SWIGLU_F32>(a, b0, b1, p, max_pairs, stream);
+    case TC_MATMUL_F32:
+      return launch_pair_mode<TC_MATMUL_F32>(a, b0, b1, p, max_pairs, stream);
+    case TC_MATMUL_F32_ACC:
+      return launch_pair_mode<TC_MATMUL_F32_ACC>(a, b0, b1, p, max_pairs, stream);
+    default:
+      return cudaErrorInvalidValue;
+  }
+}
+
+}  // namespace llk_b200

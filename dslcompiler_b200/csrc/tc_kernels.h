@@ -27,6 +27,11 @@ struct TcParams {
 };
 
 int tc_smem_bytes();
+// CTA-pair (cta_group::2) variant: m_tiles counts 256-row blocks; grid =
+// 2 x min(tiles, co-resident pairs, max_pairs if > 0).
+int tc2_smem_bytes();
+cudaError_t tc2_launch(int mode, const CUtensorMap &a, const CUtensorMap &b0, const CUtensorMap &b1,
+                       const TcParams &p, int max_pairs, cudaStream_t stream);
 int tc_threads();
 int tc_tile_n(int mode);
 cudaError_t tc_launch(int mode, const CUtensorMap &a, const CUtensorMap &b0, const CUtensorMap &b1,

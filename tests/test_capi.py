@@ -83,7 +83,9 @@ def test_plan_cache_lru_and_stats():
     llk.cache_set_max_entries(2)
     try:
         p = llk.KernelKey(N=11008, K=4096, M_bucket=4).plan(2048)
-        assert p["variant"] == capi.VARIANTS["tc"] and p["block_m"] == 128 and p["block_n"] == 128
+        # M = 2048 > 128: CTA-pair kernel, 256-row tiles x 128 Y columns
+        assert p["variant"] == capi.VARIANTS["tc"] and p["block_m"] == 256 and p["block_n"] == 128
+        assert p["grid"] % 2 == 0
         assert p["grid"] >= 1 and p["smem_bytes"] > 100 * 1024
         llk.KernelKey(N=11008, K=4096, M_bucket=4).plan(2048)
         s = llk.cache_stats()

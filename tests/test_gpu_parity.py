@@ -345,3 +345,35 @@ def test_packed_slab_layout_matches_row_major(M, K, N, variant):
     llk.synchronize(0)
     assert torch.equal(a, b)  # same kernel, same accumulation order: identical
     pw.close()
+
+
+@pytest.mark.parametrize("M,K,N,op", [(300, 512, 520, "swiglu"), (2048, 1024, 1024, "swiglu"), (513, 256, 768, "matmul")])
+def test_cta_pair_and_single_cta_kernels_agree(M, K, N, op):
+    """M > 128 runs on CTA pairs (256-row MMAs); a plan override with
+    block_m = 128 pins the one-CTA kernel.  Both must match the oracle."""
+    if op == "swiglu":
+        x, wg, wu = dg.swiglu_inputs(M, K, N, 1.0 / math.sqrt(K), 1.0, seed=M + 1)
+        ref = oracle.swiglu_fused(x, wg, wu, "f32").astype(np.float64)
+        run = lambda: llk.fused_swiglu(dev(x), dev(wg), dev(wu), out_dtype="f32", variant="tc")  # noqa: E731
+        key = llk.KernelKey(N=N, K=K, M_bucket=llk.classify_m(M), output_type=capi.LLK_DTYPE_FP32)
+    else:
+        x, wg = dg.matmul_inputs(M, K, N, seed=M + 2)
+        ref = oracle.matmul(x, wg).astype(np.float64)
+        run = lambda: llk.matmul(dev(x), dev(wg), variant="tc")  # noqa: E731
+        key = llk.KernelKey(operation=capi.LLK_OP_MATMUL, N=N, K=K, M_bucket=llk.classify_m(M),
+                            output_type=capi.LLK_DTYPE_FP32)
+    base = key.plan(M)
+    assert base["block_m"] == 256
+    y_pair = run()
+    torch.cuda.synchronize()
+    llk.synchronize(0)
+    assert rel_err(host(y_pair), ref) < 1e-5
+    single = dict(base, block_m=128, grid=148, stages=4)
+    key.insert_plan(**single)
+    try:
+        y_one = run()
+        torch.cuda.synchronize()
+        llk.synchronize(0)
+    finally:
+        key.insert_plan(**base)
+    assert rel_err(host(y_one), ref) < 1e-5
