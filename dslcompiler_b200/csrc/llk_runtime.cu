@@ -210,7 +210,7 @@ llk_launch_plan build_plan(int variant, int op, int64_t M, int64_t N, int64_t K,
     p.block_n = tc_tile_n(mode);
     p.block_k = 64;
     p.stages = pair ? 6 : 4;
-    p.split_k = 1;
+    p.split_k = pair ? 0 : 1;  // pair kernel: 0 = choose the tail split
     const int64_t tiles = ((M + p.block_m - 1) / p.block_m) * ((N + p.block_n - 1) / p.block_n);
     const int64_t ctas = pair ? 2 * tiles : tiles;
     p.grid = static_cast<int>(ctas < sm_count ? ctas : sm_count);
@@ -372,7 +372,9 @@ int launch_device(DeviceState &ds, int op, const DevTensor &x, const DevTensor &
   p.slab_major = slab ? 1 : 0;
   if (pair) {
     const int max_pairs = plan.variant == LLK_VARIANT_TC && plan.grid >= 2 ? plan.grid / 2 : 0;
-    e = tc2_launch(mode, ta, tb0, tb1, p, max_pairs, stream);
+    // plan.split_k for the pair kernel: N-split of the leftover tiles (0 = choose).
+    const int tail_split = plan.variant == LLK_VARIANT_TC ? plan.split_k : 0;
+    e = tc2_launch(mode, ta, tb0, tb1, p, max_pairs, tail_split, stream);
     return e == cudaSuccess ? LLK_OK : LLK_ERR_CUDA;
   }
   int grid = p.num_tiles < ds.sm_count ? p.num_tiles : ds.sm_count;

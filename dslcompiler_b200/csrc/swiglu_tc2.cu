@@ -24,6 +24,12 @@
 //              accumulator barriers of both CTAs.
 //   warps 2-5  epilogue in both CTAs on their own TMEM rows; each thread
 //              releases the accumulator by arriving on the leader's barrier.
+// Work split: floor(tiles / pairs) waves of whole tiles, one pair per tile;
+// the tiles left over would run as a partly idle last wave, so they are cut
+// along N into 2 or 4 narrower tiles (MMA N = 128 or 64) dealt round-robin
+// over all pairs -- the split that makes the last wave shortest.  No partial
+// sums, no fix-up: every output is still written once from TMEM.
+//
 // All waits bounded; no TMA multicast (each CTA loads its own tiles).
 #include <cuda.h>
 #include <cuda_runtime.h>
@@ -48,6 +54,29 @@ constexpr uint32_t kBBytes = 2 * kSlabBytes;        // 16 KB: this CTA's 128 col
 constexpr uint32_t kStageBytes = kABytes + kBBytes;  // 32 KB
 constexpr uint32_t kTmemCols = 512;
 constexpr uint64_t kWaitLimitNs = 2000000000ull;
+
+// One unit of a pair's work: Y columns [c0, c0 + wn) of tile `tile`.
+struct Work {
+  int tile, c0, wn;
+};
+
+// The idx-th work item of `pair` (the same sequence in every role).
+template <int TILE_N>
+__device__ __forceinline__ bool get_work(const TcParams &p, int pair, int n_pairs, int idx, Work &w) {
+  if (idx < p.dp_waves) {
+    w.tile = pair + idx * n_pairs;
+    w.c0 = 0;
+    w.wn = TILE_N;
+    return w.tile < p.num_tiles;
+  }
+  const int first_tail = p.dp_waves * n_pairs;
+  const int item = pair + (idx - p.dp_waves) * n_pairs;
+  if (item >= (p.num_tiles - first_tail) * p.tail_split) return false;
+  w.tile = first_tail + item / p.tail_split;
+  w.wn = TILE_N / p.tail_split;
+  w.c0 = (item % p.tail_split) * w.wn;
+  return true;
+}
 
 struct __align__(8) PairTail {
   uint64_t full[kStages];   // leader's copy is the one used
@@ -110,9 +139,16 @@ __global__ void __launch_bounds__(kThreads, 1)
       const uint32_t leader_full = map_shared_rank(smem_u32(&st->full[0]), 0);
       uint32_t stage = 0, phase = 0, issued = 0;
       bool ok = true;
-      for (int tile = pair; tile < p.num_tiles && ok; tile += n_pairs) {
-        const int m0 = (tile % p.m_tiles) * (2 * kRows) + static_cast<int>(rank) * kRows;
-        const int n0 = (tile / p.m_tiles) * kTileN;
+      Work w;
+      for (int idx = 0; ok && get_work<kTileN>(p, pair, n_pairs, idx, w); ++idx) {
+        const int m0 = (w.tile % p.m_tiles) * (2 * kRows) + static_cast<int>(rank) * kRows;
+        const int n0 = (w.tile / p.m_tiles) * kTileN + w.c0;
+        // B columns this CTA supplies: SwiGLU w.wn of its matrix (leader Wg,
+        // peer Wu); matmul w.wn/2, the peer's after the leader's.
+        const int cta_cols = kSwiglu ? w.wn : w.wn / 2;
+        const int nb = kSwiglu ? n0 : n0 + static_cast<int>(rank) * cta_cols;
+        const int slabs = cta_cols > 64 ? 2 : 1;
+        const uint32_t stage_tx = 2u * (kABytes + slabs * kSlabBytes);
         for (int kb = 0; kb < p.k_blocks; ++kb) {
           if (!mbar_wait_bounded(&st->empty[stage], phase ^ 1u, abort, LLK_ERR_TIMEOUT, kWaitLimitNs)) {
             ok = false;
@@ -121,18 +157,14 @@ __global__ void __launch_bounds__(kThreads, 1)
           uint8_t *sa = smem + stage * kStageBytes;
           uint8_t *sb = sa + kABytes;
           const uint32_t bar = leader_full + stage * 8u;
-          if (rank == 0) mbar_arrive_expect_tx(&st->full[stage], 2 * kStageBytes);
+          if (rank == 0) mbar_arrive_expect_tx(&st->full[stage], stage_tx);
           const int k0 = kb * kBK;
           tma_load_2d_pair(sa, &tm_a, bar, k0, m0);
-          if (kSwiglu) {
-            const CUtensorMap *w = rank == 0 ? &tm_b0 : &tm_b1;
-            tma_load_weight_slab_pair(sb, w, bar, n0, k0, p.slab_major);
-            tma_load_weight_slab_pair(sb + kSlabBytes, w, bar, n0 + 64, k0, p.slab_major);
-          } else {
-            const int nb = n0 + static_cast<int>(rank) * 128;
-            tma_load_weight_slab_pair(sb, &tm_b0, bar, nb, k0, p.slab_major);
-            tma_load_weight_slab_pair(sb + kSlabBytes, &tm_b0, bar, nb + 64, k0, p.slab_major);
-          }
+          const CUtensorMap *wmap = (kSwiglu && rank == 1) ? &tm_b1 : &tm_b0;
+          // A 32-column part still loads a whole 64-column box (the MMA reads
+          // the first 32); its start stays 64-byte aligned.
+          tma_load_weight_slab_pair(sb, wmap, bar, nb, k0, p.slab_major);
+          if (slabs == 2) tma_load_weight_slab_pair(sb + kSlabBytes, wmap, bar, nb + 64, k0, p.slab_major);
           ++issued;
           if (++stage == kStages) {
             stage = 0;
@@ -152,12 +184,13 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
   } else if (warp == 1) {
     if (lane == 0 && rank == 0) {
-      const uint32_t idesc = make_idesc_bf16_f32(2 * kRows, kMmaN, false, true);
       const uint32_t smem_base = smem_u32(smem);
       uint32_t stage = 0, phase = 0;
       bool ok = true;
-      int local = 0;
-      for (int tile = pair; tile < p.num_tiles && ok; tile += n_pairs, ++local) {
+      Work w;
+      for (int local = 0; ok && get_work<kTileN>(p, pair, n_pairs, local, w); ++local) {
+        // MMA N = the B columns of both CTAs: SwiGLU 2 x wn (gate | up), matmul wn.
+        const uint32_t idesc = make_idesc_bf16_f32(2 * kRows, kSwiglu ? 2 * w.wn : w.wn, false, true);
         const uint32_t acc = local & 1;
         if (!mbar_wait_bounded(&st->tmem_empty[acc], ((local >> 1) & 1) ^ 1u, abort, LLK_ERR_TIMEOUT,
                                kWaitLimitNs)) {
@@ -199,21 +232,21 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int q = warp & 3;
     const int row_in_tile = q * 32 + lane;
     const uint32_t leader_tmem_empty = map_shared_rank(smem_u32(&st->tmem_empty[0]), 0);
-    int local = 0;
-    for (int tile = pair; tile < p.num_tiles; tile += n_pairs, ++local) {
+    Work w;
+    for (int local = 0; get_work<kTileN>(p, pair, n_pairs, local, w); ++local) {
       const uint32_t acc = local & 1;
       if (!mbar_wait_bounded(&st->tmem_full[acc], (local >> 1) & 1, abort, LLK_ERR_TIMEOUT, kWaitLimitNs)) break;
       tc_fence_after();
-      const int m0 = (tile % p.m_tiles) * (2 * kRows) + static_cast<int>(rank) * kRows;
-      const int n0 = (tile / p.m_tiles) * kTileN;
+      const int m0 = (w.tile % p.m_tiles) * (2 * kRows) + static_cast<int>(rank) * kRows;
+      const int n0 = (w.tile / p.m_tiles) * kTileN + w.c0;
       const int row = m0 + row_in_tile;
       const uint32_t t_row = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + acc * kMmaN;
       if (kSwiglu) {
 #pragma unroll 1
-        for (int c = 0; c < 128; c += 32) {
+        for (int c = 0; c < w.wn; c += 32) {
           uint32_t g[32], u[32];
           tmem_ld_32x32b_x32(t_row + c, g);
-          tmem_ld_32x32b_x32(t_row + 128 + c, u);
+          tmem_ld_32x32b_x32(t_row + w.wn + c, u);
           tmem_ld_wait();
           const int col = n0 + c;
           if (row < p.M && col < p.N) {
@@ -249,7 +282,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
       } else {
 #pragma unroll 1
-        for (int c = 0; c < 256; c += 32) {
+        for (int c = 0; c < w.wn; c += 32) {
           uint32_t r[32];
           tmem_ld_32x32b_x32(t_row + c, r);
           tmem_ld_wait();
@@ -300,8 +333,8 @@ __global__ void __launch_bounds__(kThreads, 1)
 }
 
 template <int MODE>
-cudaError_t launch_pair_mode(const CUtensorMap &a, const CUtensorMap &b0, const CUtensorMap &b1, const TcParams &p,
-                             int max_pairs, cudaStream_t stream) {
+cudaError_t launch_pair_mode(const CUtensorMap &a, const CUtensorMap &b0, const CUtensorMap &b1, TcParams p,
+                             int max_pairs, int tail_split, cudaStream_t stream) {
   auto kern = tc2_kernel<MODE>;
   const int smem = tc2_smem_bytes();
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
@@ -324,8 +357,29 @@ cudaError_t launch_pair_mode(const CUtensorMap &a, const CUtensorMap &b0, const 
     cudaGetLastError();
     clusters = 1;
   }
-  int pairs = p.num_tiles < clusters ? p.num_tiles : clusters;
+  int pairs = clusters;
   if (max_pairs >= 1 && pairs > max_pairs) pairs = max_pairs;
+  // Whole-tile waves, then the leftover tiles cut into g column parts: the
+  // last wave takes ceil(left * g / pairs) / g tile-times; pick the g that
+  // makes it shortest (ties: the wider tiles).
+  p.dp_waves = p.num_tiles / pairs;
+  const int left = p.num_tiles - p.dp_waves * pairs;
+  int g = 1;
+  if (tail_split == 1 || tail_split == 2 || tail_split == 4) {
+    g = tail_split;
+  } else if (left > 0) {
+    double best = 1e30;
+    for (int cand = 1; cand <= 4; cand *= 2) {
+      const double t = static_cast<double>((left * cand + pairs - 1) / pairs) / cand;
+      if (t < best - 1e-9) {
+        best = t;
+        g = cand;
+      }
+    }
+  }
+  p.tail_split = g;
+  // No pair without work: at most all tiles' parts.
+  if (p.dp_waves == 0 && pairs > left * g) pairs = left * g;
   cfg.gridDim = dim3(2 * pairs);
   e = cudaLaunchKernelEx(&cfg, kern, a, b0, b1, p);
   if (e != cudaSuccess) return e;
@@ -336,17 +390,17 @@ cudaError_t launch_pair_mode(const CUtensorMap &a, const CUtensorMap &b0, const 
 
 int tc2_smem_bytes() { return kStages * kStageBytes + static_cast<int>(sizeof(PairTail)) + 1024; }
 
-cudaError_t tc2_launch(int mode, const CUtensorMap &a, const CUtensorMap &b0, const CUtensorMap &b1,
-                       const TcParams &p, int max_pairs, cudaStream_t stream) {
+cudaError_t tc2_launch(int mode, const CUtensorMap &a, const CUtensorMap &b0, const CUtensorMap &b1, TcParams p,
+                       int max_pairs, int tail_split, cudaStream_t stream) {
   switch (mode) {
     case TC_SWIGLU_BF16:
-      return launch_pair_mode<TC_SWIGLU_BF16>(a, b0, b1, p, max_pairs, stream);
+      return launch_pair_mode<TC_SWIGLU_BF16>(a, b0, b1, p, max_pairs, tail_split, stream);
     case TC_SWIGLU_F32:
-      return launch_pair_mode<TC_SWIGLU_F32>(a, b0, b1, p, max_pairs, stream);
+      return launch_pair_mode<TC_SWIGLU_F32>(a, b0, b1, p, max_pairs, tail_split, stream);
     case TC_MATMUL_F32:
-      return launch_pair_mode<TC_MATMUL_F32>(a, b0, b1, p, max_pairs, stream);
+      return launch_pair_mode<TC_MATMUL_F32>(a, b0, b1, p, max_pairs, tail_split, stream);
     case TC_MATMUL_F32_ACC:
-      return launch_pair_mode<TC_MATMUL_F32_ACC>(a, b0, b1, p, max_pairs, stream);
+      return launch_pair_mode<TC_MATMUL_F32_ACC>(a, b0, b1, p, max_pairs, tail_split, stream);
     default:
       return cudaErrorInvalidValue;
   }

@@ -24,14 +24,20 @@ struct TcParams {
   uint32_t b_lbo;     // MN-major B descriptor: bytes between 64-column slabs
   uint32_t b_sbo;     // MN-major B descriptor: bytes between 8-row k groups
   int slab_major;     // B tensor maps describe slab-major packed weights (3-D)
+  // CTA-pair kernel work split (filled by tc2_launch): dp_waves waves of
+  // whole tiles, one pair per tile; the tiles left over are cut along N into
+  // tail_split narrower tiles (1, 2 or 4) dealt round-robin over the pairs.
+  int dp_waves;
+  int tail_split;
 };
 
 int tc_smem_bytes();
 // CTA-pair (cta_group::2) variant: m_tiles counts 256-row blocks; grid =
-// 2 x min(tiles, co-resident pairs, max_pairs if > 0).
+// 2 x min(tiles, co-resident pairs, max_pairs if > 0).  tail_split: 0 =
+// choose, 1/2/4 = cut the leftover tiles into that many column parts.
 int tc2_smem_bytes();
 cudaError_t tc2_launch(int mode, const CUtensorMap &a, const CUtensorMap &b0, const CUtensorMap &b1,
-                       const TcParams &p, int max_pairs, cudaStream_t stream);
+                       TcParams p, int max_pairs, int tail_split, cudaStream_t stream);
 int tc_threads();
 int tc_tile_n(int mode);
 cudaError_t tc_launch(int mode, const CUtensorMap &a, const CUtensorMap &b0, const CUtensorMap &b1,

@@ -347,7 +347,8 @@ def test_packed_slab_layout_matches_row_major(M, K, N, variant):
     pw.close()
 
 
-@pytest.mark.parametrize("M,K,N,op", [(300, 512, 520, "swiglu"), (2048, 1024, 1024, "swiglu"), (513, 256, 768, "matmul")])
+@pytest.mark.parametrize("M,K,N,op", [(300, 512, 520, "swiglu"), (2048, 1024, 1024, "swiglu"), (513, 256, 768, "matmul"),
+                                      (1000, 256, 1400, "matmul"), (700, 320, 1408, "swiglu")])
 def test_cta_pair_and_single_cta_kernels_agree(M, K, N, op):
     """M > 128 runs on CTA pairs (256-row MMAs); a plan override with
     block_m = 128 pins the one-CTA kernel.  Both must match the oracle."""
@@ -368,6 +369,16 @@ def test_cta_pair_and_single_cta_kernels_agree(M, K, N, op):
     torch.cuda.synchronize()
     llk.synchronize(0)
     assert rel_err(host(y_pair), ref) < 1e-5
+    # leftover tiles cut into 1, 2 or 4 column parts (MMA N 256 / 128 / 64)
+    for split in (1, 2, 4):
+        key.insert_plan(**dict(base, split_k=split, grid=2 * 7))  # 7 pairs: every shape leaves a tail
+        try:
+            y_split = run()
+            torch.cuda.synchronize()
+            llk.synchronize(0)
+        finally:
+            key.insert_plan(**base)
+        assert torch.equal(y_split, y_pair), split  # same per-element accumulation order
     single = dict(base, block_m=128, grid=148, stages=4)
     key.insert_plan(**single)
     try:
