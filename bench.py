@@ -320,6 +320,8 @@ def our_arm(args):
     pw.close()
 
     extras = {}
+    if world > 1:
+        extras["gather_y"] = gather_timing(args, dev, stream, yd, N, world, barrier, max_over_ranks)
     cpu = None
     if world == 1 and not args.quick:
         extras = single_gpu_extras(args, dev, stream, flush, peak_tf, peak_gbs)
@@ -355,6 +357,38 @@ def our_arm(args):
         dist.barrier(device_ids=[local])
         dist.destroy_process_group()
     return 0
+
+
+def gather_timing(args, dev, stream, yd, N, world, barrier, max_over_ranks):
+    """Optional full-Y path: NCCL all-gather of the padded shards plus the
+    llk_gather_columns relayout -- timed apart from the kernel."""
+    import torch
+    import torch.distributed as dist
+
+    from dslcompiler_b200.sharding import gather_columns, shard_bounds
+
+    bounds = shard_bounds(N, world)
+    width = max(e - b for b, e in bounds)
+    M = yd.shape[0]
+    buf = torch.zeros((M, width), dtype=yd.dtype, device=dev)
+    buf[:, : yd.shape[1]].copy_(yd)
+    gathered = torch.empty((world, M, width), dtype=yd.dtype, device=dev)
+    y_full = torch.empty((M, N), dtype=yd.dtype, device=dev)
+
+    def step():
+        dist.all_gather_into_tensor(gathered, buf)
+        gather_columns(gathered, bounds, y_full)
+
+    for _ in range(3):
+        step()
+    torch.cuda.synchronize()
+    barrier()
+    steps = max(5, min(args.steps, 50))
+    t = time_steps(step, None, steps, stream)
+    ms = max_over_ranks(sum(t)) / steps
+    recv = (world - 1) * M * width * yd.element_size()
+    return {"ms": ms, "bytes_received_per_gpu": recv, "GB/s_per_gpu": recv / (ms * 1e-3) / 1e9,
+            "what": "all_gather_into_tensor (NCCL) of padded Y shards + llk_gather_columns relayout"}
 
 
 def single_gpu_extras(args, dev, stream, flush, peak_tf, peak_gbs):

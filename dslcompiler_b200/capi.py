@@ -103,6 +103,7 @@ PROTOTYPES = {
     "llk_packed_weights_info": (_i, [_vp, _P(_i64), _P(_i64), _P(_i64)]),
     "llk_swiglu_packed": (_i, [_P(Tensor2D), _vp, _P(Tensor2D), _P(KernelContext), _P(GpuContext)]),
     "llk_shard_columns": (_i, [_i64, _i, _i, _P(_i64), _P(_i64)]),
+    "llk_gather_columns": (_i, [_vp, _i, _i64, _i64, _P(_i64), _vp, _i64, _i, _P(GpuContext)]),
     "llk_cuda_probe": (_i, [_i, _P(CudaTarget)]),
     "llk_kernel_key_hash": (_u64, [_P(KernelKeyC)]),
     "llk_plan_lookup": (_i, [_P(KernelKeyC), _i64, _P(LaunchPlan)]),

@@ -205,6 +205,16 @@ int llk_swiglu_packed(const Tensor2D *x, const llk_packed_weights *pw, Tensor2D 
  * (earlier shards take the remainder).  Returns LLK_ERR_ARG on bad input. */
 int llk_shard_columns(int64_t N, int n_shards, int index, int64_t *begin, int64_t *end);
 
+/* After an all-gather of equal-width (padded) column shards, shard-major
+ * `shards` = [n_shards][M][width] (device, elem_bytes 2 = bf16 or 4 = f32)
+ * holds shard s's columns [begins[s], begins[s+1]) in its first
+ * begins[s+1]-begins[s] columns; writes them into row-major device Y
+ * (row stride ldy elements).  begins: host array of n_shards + 1 offsets,
+ * n_shards <= 64.  Asynchronous on gpu->stream.  No counterpart in the
+ * reference (it has no multi-device path). */
+int llk_gather_columns(const void *shards, int n_shards, int64_t M, int64_t width, const int64_t *begins, void *y,
+                       int64_t ldy, int elem_bytes, const llk_gpu_context *gpu);
+
 /* ---- target probe (analogue of lib/Target/X86/TargetAVX2.cpp:33-92) ---- */
 
 typedef struct llk_cuda_target {
