@@ -1,0 +1,187 @@
+"""The compiler-side tools on CPU: LLK parsing + the reference verifier
+rules, the LLK -> micro lowering, the MachineModel loader/validation, the
+micro-perf L0 bound, the schedule DB loader and the CLI entry points."""
+import json
+import os
+import subprocess
+import sys
+
+import pytest
+import yaml
+
+from dslcompiler_b200 import compiler, microperf, schedule
+from tests.conftest import ROOT
+
+MACHINE = os.path.join(ROOT, "dslcompiler_b200", "machines", "b200-sm100a.yaml")
+
+SWIGLU = """
+func.func @f(%x: tensor<{M}x{K}xbf16>, %wg: tensor<{K}x{N}xbf16>, %wu: tensor<{K}x{N2}xbf16>, %init: tensor<{M}x{N}xbf16>) -> tensor<{M}x{N}xbf16> {{
+  %y = llk.fused_swiglu ins(%x, %wg, %wu : tensor<{M}x{K}xbf16>, tensor<{K}x{N}xbf16>, tensor<{K}x{N2}xbf16>)
+      outs(%init : tensor<{M}x{N}xbf16>)
+      {{accumulator_type = f32, activation = #llk.activation<silu>, math_mode = #llk.math_mode<bounded_fast>}}
+      -> tensor<{M}x{N}xbf16>
+  return %y : tensor<{M}x{N}xbf16>
+}}
+"""
+
+DYN = """
+  %y = llk.fused_swiglu ins(%x, %wg, %wu : tensor<?x?xbf16>, tensor<?x?xbf16>, tensor<?x?xbf16>)
+      outs(%init : tensor<?x?xbf16>)
+      {accumulator_type = f32, activation = #llk.activation<silu>, math_mode = #llk.math_mode<strict>}
+      -> tensor<?x?xbf16>
+"""
+
+MATMUL = """
+  %0 = llk.matmul ins(%a, %b : tensor<4096x4096xbf16>, tensor<4096x4096xbf16>)
+      outs(%c : tensor<4096x4096xf32>) {accumulator_type = f32, math_mode = #llk.math_mode<strict>}
+      -> tensor<4096x4096xf32>
+"""
+
+
+def test_parse_and_verify_static():
+    ops = compiler.parse_llk(SWIGLU.format(M=2048, K=4096, N=11008, N2=11008))
+    assert len(ops) == 1 and ops[0].op == "fused_swiglu"
+    compiler.verify(ops[0])
+    assert compiler.resolve_shape(ops[0]) == (2048, 11008, 4096)
+    assert "math_mode" in ops[0].attrs
+
+
+def test_verifier_rules_match_reference_messages():
+    # LLKOps.cpp:69-81: "N dimension mismatch between Wg=... and Wu=..."
+    op = compiler.parse_llk(SWIGLU.format(M=8, K=64, N=128, N2=96))[0]
+    with pytest.raises(compiler.VerifyError, match="N dimension mismatch between Wg=128 and Wu=96"):
+        compiler.verify(op)
+
+
+def test_dynamic_dims_need_flags():
+    op = compiler.parse_llk(DYN)[0]
+    compiler.verify(op)
+    with pytest.raises(compiler.VerifyError, match="dynamic"):
+        compiler.resolve_shape(op)
+    assert compiler.resolve_shape(op, 4, 14336, 4096) == (4, 14336, 4096)
+
+
+@pytest.mark.parametrize("M,variant,candidate", [(2048, "auto", "tc2_kernel"), (64, "tc", "tc_swiglu_kernel"),
+                                                  (4, "auto", "decode_kernel")])
+def test_lowering_picks_the_dispatched_kernel(M, variant, candidate):
+    op = compiler.parse_llk(DYN)[0]
+    low = compiler.lower_to_micro(op, M, 14336, 4096, variant)
+    assert f'candidate = "{candidate}' in low.text and 'target = "b200-sm100a"' in low.text
+    assert low.text.count("{") == low.text.count("}")
+
+
+def test_l0_bound_counts_work_exactly():
+    machine = microperf.load_machine(MACHINE)
+    op = compiler.parse_llk(SWIGLU.format(M=2048, K=4096, N=11008, N2=11008))[0]
+    rep = microperf.l0_bound(compiler.lower_to_micro(op, 2048, 11008, 4096).text, machine)
+    assert rep.total_flops == 4 * 2048 * 4096 * 11008
+    assert rep.compulsory_dram_bytes == 2 * 2048 * 4096 + 4 * 4096 * 11008 + 2 * 2048 * 11008
+    assert rep.bottleneck == "matrix_engine"
+    # 3.694e11 FLOP / (148 SMs x 8192 FLOP/cycle)
+    assert abs(rep.compute_cycles - 4 * 2048 * 4096 * 11008 / (148 * 8192)) < 1
+    decode = compiler.lower_to_micro(compiler.parse_llk(DYN)[0], 1, 14336, 4096, "decode").text
+    rep = microperf.l0_bound(decode, machine)
+    assert rep.bottleneck == "dram_bandwidth"
+
+
+def test_machine_model_validation_rules():
+    d = yaml.safe_load(open(MACHINE))
+    microperf.validate_machine(d)
+    for mutate, msg in [(lambda d: d.pop("schema_version"), "schema_version"),
+                        (lambda d: d.update(schema_version=2), "unsupported schema"),
+                        (lambda d: d.update(clock_hz=0), "zero clock"),
+                        (lambda d: d["memory"]["dram"].update(bandwidth_bytes_per_cycle=0), "bandwidth"),
+                        (lambda d: d["compute"]["matrix_engines"][0].update(tile_shapes=[[1, 2]]), "length 3"),
+                        (lambda d: d["compute"]["matrix_engines"][0].update(input_dtypes=["f64x"]), "unknown dtype"),
+                        (lambda d: d["memory"].pop("acc"), "missing memory")]:
+        bad = yaml.safe_load(open(MACHINE))
+        mutate(bad)
+        with pytest.raises(microperf.MachineModelError, match=msg):
+            microperf.validate_machine(bad)
+
+
+def test_schedule_db_is_target_and_shape_aware(tmp_path):
+    p = tmp_path / "db.json"
+    json.dump({"version": 1, "entries": [
+        {"operation": "fused_swiglu", "target": "x86-avx2", "shape": {"M_bucket": 4, "N": 11008, "K": 4096},
+         "dtype": "bf16", "math_mode": "bounded_fast", "schedule": {"BM": 32, "BN": 64, "BK": 64}},
+        {"operation": "fused_swiglu", "target": "b200-sm100a", "shape": {"M_bucket": 4, "N": 11008, "K": 4096},
+         "dtype": "bf16", "math_mode": "strict", "schedule": {"variant": "tc", "block_m": 256}, "measured_gflops": 5.0},
+        {"operation": "fused_swiglu", "target": "b200-sm100a", "shape": {"M_bucket": 4, "N": 11008, "K": 4096},
+         "dtype": "bf16", "math_mode": "strict", "schedule": {"variant": "tc", "block_m": 128}, "measured_gflops": 9.0},
+        {"operation": "fused_swiglu", "target": "b200-sm100a", "shape": {"M_bucket": 4, "N": 4096, "K": 4096},
+         "schedule": {}},
+        {"broken": True}]}, open(p, "w"))
+    hits = schedule.load(str(p), 4, 11008, 4096)
+    assert [h.schedule["block_m"] for h in hits] == [128, 256]  # best measured first, AVX2 entry excluded
+    assert schedule.load(str(p), 4, 11008, 2048) == []
+    assert len(schedule.load(str(p), 4, 11008, 4096, target="x86-avx2")) == 1
+    e = schedule.ScheduleEntry("fused_swiglu", "b200-sm100a", 4, 11008, 4096, schedule={"variant": "tc", "block_m": 256})
+    schedule.write_db([e], str(p), merge=True)
+    assert len(schedule.read_db(str(p))) == 3  # replaced the two same-key entries, kept the others
+
+
+def test_shipped_schedule_db_entries_are_installable():
+    n = schedule.install(schedule.DEFAULT_DB)
+    assert n >= 1
+
+
+def _run(args):
+    return subprocess.run([sys.executable, "-m"] + args, capture_output=True, text=True, cwd=ROOT, timeout=120)
+
+
+def test_llk_compile_cli(tmp_path):
+    f = tmp_path / "in.mlir"
+    f.write_text(SWIGLU.format(M=2048, K=4096, N=11008, N2=11008))
+    r = _run(["dslcompiler_b200.cli.llk_compile", str(f), "--emit", "micro"])
+    assert r.returncode == 0 and r.stdout.strip().endswith("Compilation successful")
+    assert "micro.kernel @fused_swiglu_M2048_N11008_K4096" in r.stdout
+    bad = tmp_path / "bad.mlir"
+    bad.write_text(SWIGLU.format(M=8, K=64, N=128, N2=96))
+    r = _run(["dslcompiler_b200.cli.llk_compile", str(bad)])
+    assert r.returncode == 1 and "Compilation pipeline failed" in r.stderr
+    empty = tmp_path / "e.mlir"
+    empty.write_text("module {}")
+    r = _run(["dslcompiler_b200.cli.llk_compile", str(empty)])
+    assert r.returncode == 1 and "Failed to parse" in r.stderr
+    m = tmp_path / "mm.mlir"
+    m.write_text(MATMUL)
+    out = tmp_path / "mm.micro.mlir"
+    r = _run(["dslcompiler_b200.cli.llk_compile", str(m), "--emit", "micro", "-o", str(out)])
+    assert r.returncode == 0
+    r = _run(["dslcompiler_b200.cli.micro_perf", str(out), "--format", "yaml"])
+    rep = yaml.safe_load(r.stdout)
+    assert rep["total_flops"] == 2 * 4096 ** 3 and rep["machine"] == "b200-sm100a"
+
+
+def test_llk_tune_dry_run_writes_schedule_entries(tmp_path):
+    out = tmp_path / "tune.json"
+    r = _run(["dslcompiler_b200.cli.llk_tune", "--M", "2048", "--N", "11008", "--K", "4096", "--dry-run", "-o", str(out)])
+    assert r.returncode == 0 and "Wrote top-3 configs" in r.stdout
+    ents = schedule.read_db(str(out))
+    assert len(ents) == 3 and all(e.target == "b200-sm100a" and e.M_bucket == 4 for e in ents)
+
+
+def test_llk_bench_cpu_mode():
+    r = _run(["dslcompiler_b200.cli.llk_bench", "--M", "8", "--N", "256", "--K", "256", "--threads", "2",
+              "--warmup-ms", "10", "--measure-ms", "50", "--reps", "2", "--cpu"])
+    assert r.returncode == 0
+    assert r.stdout.splitlines()[0].startswith("LLK Bench")
+    assert "Best:" in r.stdout and "GFLOPS" in r.stdout
+
+
+@pytest.mark.gpu
+def test_llk_bench_and_tune_on_gpu(tmp_path):
+    torch = pytest.importorskip("torch")
+    if not torch.cuda.is_available():
+        pytest.skip("no GPU")
+    r = _run(["dslcompiler_b200.cli.llk_bench", "--M", "512", "--N", "2048", "--K", "1024", "--warmup-ms", "20",
+              "--measure-ms", "50", "--reps", "2", "--json"])
+    assert r.returncode == 0, r.stderr
+    rec = json.loads(r.stdout.strip().splitlines()[-1])
+    assert rec["gflops"] > 1000  # a real tensor-core kernel, not a stand-in loop
+    out = tmp_path / "t.json"
+    r = _run(["dslcompiler_b200.cli.llk_tune", "--M", "8", "--N", "2048", "--K", "1024", "--iters", "3", "-o", str(out)])
+    assert r.returncode == 0, r.stderr
+    ents = schedule.read_db(str(out))
+    assert len(ents) == 3 and all(e.measured_gflops > 0 for e in ents)
