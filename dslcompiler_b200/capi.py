@@ -79,7 +79,7 @@ class KernelKeyC(ctypes.Structure):
 
 class LaunchPlan(ctypes.Structure):
     _fields_ = [(n, ctypes.c_int) for n in ("variant", "block_m", "block_n", "block_k", "stages", "split_k", "grid",
-                                            "threads", "smem_bytes")]
+                                            "threads", "smem_bytes", "sched")]
 
 
 # Every exported symbol with its prototype: (restype, argtypes).

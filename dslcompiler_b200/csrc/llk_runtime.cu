@@ -211,6 +211,9 @@ llk_launch_plan build_plan(int variant, int op, int64_t M, int64_t N, int64_t K,
     p.block_k = 64;
     p.stages = pair ? 6 : 4;
     p.split_k = pair ? 0 : 1;  // pair kernel: 0 = choose the tail split
+    // Static round-robin tiles: measured 3-5 % faster than the dynamic work
+    // counter (interleaved A/B on configs 2 and 3 and on 8-GPU shards).
+    p.sched = 1;
     const int64_t tiles = ((M + p.block_m - 1) / p.block_m) * ((N + p.block_n - 1) / p.block_n);
     const int64_t ctas = pair ? 2 * tiles : tiles;
     p.grid = static_cast<int>(ctas < sm_count ? ctas : sm_count);
@@ -374,7 +377,21 @@ int launch_device(DeviceState &ds, int op, const DevTensor &x, const DevTensor &
     const int max_pairs = plan.variant == LLK_VARIANT_TC && plan.grid >= 2 ? plan.grid / 2 : 0;
     // plan.split_k for the pair kernel: N-split of the leftover tiles (0 = choose).
     const int tail_split = plan.variant == LLK_VARIANT_TC ? plan.split_k : 0;
-    e = tc2_launch(mode, ta, tb0, tb1, p, max_pairs, tail_split, stream);
+    // Dynamic work distribution needs one zeroed device int: the caller's
+    // scratch (cleared here) or the library workspace (kept at zero by every
+    // launch).  plan.sched = 1 selects the static schedule.
+    int *counter = nullptr;
+    if (plan.variant == LLK_VARIANT_TC && plan.sched == 0) {
+      if (scratch != nullptr) {
+        if (scratch_bytes < kTc2SchedBytes) return LLK_ERR_NOMEM;
+        if (cudaMemsetAsync(scratch, 0, sizeof(int), stream) != cudaSuccess) return LLK_ERR_CUDA;
+        counter = static_cast<int *>(scratch);
+      } else {
+        if (ds.workspace.ensure(kTc2SchedBytes, true) != cudaSuccess) return LLK_ERR_NOMEM;
+        counter = static_cast<int *>(ds.workspace.ptr);
+      }
+    }
+    e = tc2_launch(mode, ta, tb0, tb1, p, max_pairs, tail_split, counter, stream);
     return e == cudaSuccess ? LLK_OK : LLK_ERR_CUDA;
   }
   int grid = p.num_tiles < ds.sm_count ? p.num_tiles : ds.sm_count;

@@ -297,4 +297,40 @@ __device__ __forceinline__ void tc_commit_pair_mc(uint64_t *bar, uint16_t cta_ma
 }
 
 
+
+// Wait on a barrier that other CTAs of the cluster arrive on, with
+// cluster-scope acquire (makes their shared::cluster stores visible).
+__device__ __forceinline__ bool mbar_try_wait_cluster(uint64_t *bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+
+__device__ __forceinline__ bool mbar_wait_cluster_bounded(uint64_t *bar, uint32_t parity, volatile int *abort,
+                                                          int code, uint64_t limit_ns) {
+  if (mbar_try_wait_cluster(bar, parity)) return true;
+  const uint64_t t0 = global_timer_ns();
+  for (uint32_t i = 1;; ++i) {
+    if (mbar_try_wait_cluster(bar, parity)) return true;
+    if ((i & 63u) == 0) {
+      if (*abort != 0) return false;
+      if (global_timer_ns() - t0 > limit_ns) {
+        *abort = code;
+        return false;
+      }
+    }
+  }
+}
+
+// 32-bit store into another CTA's shared memory (shared::cluster address).
+__device__ __forceinline__ void st_shared_cluster_u32(uint32_t cluster_addr, uint32_t v) {
+  asm volatile("st.shared::cluster.u32 [%0], %1;" ::"r"(cluster_addr), "r"(v) : "memory");
+}
+
 }  // namespace llk_b200

@@ -60,25 +60,38 @@ struct Work {
   int tile, c0, wn;
 };
 
-// The idx-th work item of `pair` (the same sequence in every role).
+// Work item `item` of the launch: items [0, whole) are whole tiles (whole =
+// dp_waves x pairs), the rest are the tail_split column parts of the
+// leftover tiles.  False past the last item.
 template <int TILE_N>
-__device__ __forceinline__ bool get_work(const TcParams &p, int pair, int n_pairs, int idx, Work &w) {
-  if (idx < p.dp_waves) {
-    w.tile = pair + idx * n_pairs;
+__device__ __forceinline__ bool item_to_work(const TcParams &p, int n_pairs, int item, Work &w) {
+  const int whole = p.dp_waves * n_pairs;
+  if (item < whole) {
+    w.tile = item;
     w.c0 = 0;
     w.wn = TILE_N;
-    return w.tile < p.num_tiles;
+    return true;
   }
-  const int first_tail = p.dp_waves * n_pairs;
-  const int item = pair + (idx - p.dp_waves) * n_pairs;
-  if (item >= (p.num_tiles - first_tail) * p.tail_split) return false;
-  w.tile = first_tail + item / p.tail_split;
+  const int j = item - whole;
+  if (j >= (p.num_tiles - whole) * p.tail_split) return false;
+  w.tile = whole + j / p.tail_split;
   w.wn = TILE_N / p.tail_split;
-  w.c0 = (item % p.tail_split) * w.wn;
+  w.c0 = (j % p.tail_split) * w.wn;
   return true;
 }
 
+// Static schedule: pair `pair` takes items pair, pair + pairs, ...
+template <int TILE_N>
+__device__ __forceinline__ bool get_work(const TcParams &p, int pair, int n_pairs, int idx, Work &w) {
+  return item_to_work<TILE_N>(p, n_pairs, pair + idx * n_pairs, w);
+}
+
+constexpr int kRing = 8;  // work items in flight between the leader's draw and the last role reading it
+
 struct __align__(8) PairTail {
+  uint64_t sched_full[kRing];   // both CTAs: an item index was posted in sched_ring
+  uint64_t sched_empty[kRing];  // leader: all 10 readers of the pair took the slot
+  int sched_ring[kRing];
   uint64_t full[kStages];   // leader's copy is the one used
   uint64_t empty[kStages];  // both CTAs
   uint64_t tmem_full[2];    // both CTAs
@@ -87,6 +100,65 @@ struct __align__(8) PairTail {
   uint32_t tmem_base;
   int abort;
 };
+
+enum Role { ROLE_PRODUCER = 0, ROLE_MMA = 1, ROLE_EPILOGUE = 2 };
+
+// The i-th work item of this pair for one role.  Static schedule: computed.
+// Dynamic schedule: the leader's producer draws the next item index from the
+// launch-wide counter and posts it in ring slot i % kRing of both CTAs; every
+// other role of the pair (peer producer, leader MMA thread, the 8 epilogue
+// warps) waits for the slot, copies the index and releases the slot on the
+// leader.  All waits bounded; `ok` turns false when one gives up.
+template <int TILE_N>
+__device__ __forceinline__ bool next_work(const TcParams &p, PairTail *st, uint32_t rank, int role, int pair,
+                                          int n_pairs, int i, Work &w, volatile int *abort, bool &ok,
+                                          int &posted, bool &drew_end) {
+  if (!p.dynamic) return get_work<TILE_N>(p, pair, n_pairs, i, w);
+  const int slot = i % kRing;
+  const uint32_t ph = static_cast<uint32_t>(i / kRing) & 1u;
+  int idx;
+  if (role == ROLE_PRODUCER && rank == 0) {
+    // Keep one item posted ahead of the one starting, so the counter's round
+    // trip and the hand-off to the peer overlap the current item's loads.
+    while (!drew_end && posted <= i + 1) {
+      const int ps = posted % kRing;
+      const uint32_t pph = static_cast<uint32_t>(posted / kRing) & 1u;
+      if (!mbar_wait_bounded(&st->sched_empty[ps], pph ^ 1u, abort, LLK_ERR_TIMEOUT, kWaitLimitNs)) {
+        ok = false;
+        return false;
+      }
+      const int d = atomicAdd(p.sched_counter, 1);
+      st->sched_ring[ps] = d;
+      st_shared_cluster_u32(map_shared_rank(smem_u32(&st->sched_ring[ps]), 1), static_cast<uint32_t>(d));
+      mbar_arrive(&st->sched_full[ps]);
+      mbar_arrive_cluster(map_shared_rank(smem_u32(&st->sched_full[ps]), 1));
+      ++posted;
+      if (d >= p.n_items) {
+        drew_end = true;
+        // Every pair draws exactly one index past the end; the last of those
+        // draws is the launch's last use of the counter: leave it at zero.
+        if (d == p.n_items + n_pairs - 1) atomicExch(p.sched_counter, 0);
+      }
+    }
+    if (i >= posted) return false;
+    idx = st->sched_ring[slot];
+  } else {
+    if (!mbar_wait_cluster_bounded(&st->sched_full[slot], ph, abort, LLK_ERR_TIMEOUT, kWaitLimitNs)) {
+      ok = false;
+      return false;
+    }
+    idx = *reinterpret_cast<volatile int *>(&st->sched_ring[slot]);
+    const uint32_t leader_empty = map_shared_rank(smem_u32(&st->sched_empty[slot]), 0);
+    if (role == ROLE_EPILOGUE) {
+      __syncwarp();
+      if ((threadIdx.x & 31) == 0) mbar_arrive_cluster(leader_empty);
+    } else {
+      mbar_arrive_cluster(leader_empty);
+    }
+  }
+  if (idx >= p.n_items) return false;
+  return item_to_work<TILE_N>(p, n_pairs, idx, w);
+}
 
 template <int MODE>
 __global__ void __launch_bounds__(kThreads, 1)
@@ -115,6 +187,10 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(&st->tmem_empty[a], 256);
     }
     mbar_init(&st->mma_done, 1);
+    for (int r = 0; r < kRing; ++r) {
+      mbar_init(&st->sched_full[r], 1);
+      mbar_init(&st->sched_empty[r], 10);  // peer producer + leader MMA + 8 epilogue warps
+    }
     st->abort = 0;
     fence_mbar_init();
   }
@@ -140,7 +216,10 @@ __global__ void __launch_bounds__(kThreads, 1)
       uint32_t stage = 0, phase = 0, issued = 0;
       bool ok = true;
       Work w;
-      for (int idx = 0; ok && get_work<kTileN>(p, pair, n_pairs, idx, w); ++idx) {
+      int posted = 0;
+      bool drew_end = false;
+      for (int idx = 0; ok && next_work<kTileN>(p, st, rank, ROLE_PRODUCER, pair, n_pairs, idx, w, abort, ok, posted, drew_end);
+           ++idx) {
         const int m0 = (w.tile % p.m_tiles) * (2 * kRows) + static_cast<int>(rank) * kRows;
         const int n0 = (w.tile / p.m_tiles) * kTileN + w.c0;
         // B columns this CTA supplies: SwiGLU w.wn of its matrix (leader Wg,
@@ -188,7 +267,10 @@ __global__ void __launch_bounds__(kThreads, 1)
       uint32_t stage = 0, phase = 0;
       bool ok = true;
       Work w;
-      for (int local = 0; ok && get_work<kTileN>(p, pair, n_pairs, local, w); ++local) {
+      int posted = 0;
+      bool drew_end = false;
+      for (int local = 0; ok && next_work<kTileN>(p, st, rank, ROLE_MMA, pair, n_pairs, local, w, abort, ok, posted, drew_end);
+           ++local) {
         // MMA N = the B columns of both CTAs: SwiGLU 2 x wn (gate | up), matmul wn.
         const uint32_t idesc = make_idesc_bf16_f32(2 * kRows, kSwiglu ? 2 * w.wn : w.wn, false, true);
         const uint32_t acc = local & 1;
@@ -233,7 +315,11 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int row_in_tile = q * 32 + lane;
     const uint32_t leader_tmem_empty = map_shared_rank(smem_u32(&st->tmem_empty[0]), 0);
     Work w;
-    for (int local = 0; get_work<kTileN>(p, pair, n_pairs, local, w); ++local) {
+    bool ok = true;
+    int posted = 0;
+    bool drew_end = false;
+    for (int local = 0; ok && next_work<kTileN>(p, st, rank, ROLE_EPILOGUE, pair, n_pairs, local, w, abort, ok, posted, drew_end);
+         ++local) {
       const uint32_t acc = local & 1;
       if (!mbar_wait_bounded(&st->tmem_full[acc], (local >> 1) & 1, abort, LLK_ERR_TIMEOUT, kWaitLimitNs)) break;
       tc_fence_after();
@@ -334,7 +420,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 
 template <int MODE>
 cudaError_t launch_pair_mode(const CUtensorMap &a, const CUtensorMap &b0, const CUtensorMap &b1, TcParams p,
-                             int max_pairs, int tail_split, cudaStream_t stream) {
+                             int max_pairs, int tail_split, int *sched_counter, cudaStream_t stream) {
   auto kern = tc2_kernel<MODE>;
   const int smem = tc2_smem_bytes();
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
@@ -380,6 +466,9 @@ cudaError_t launch_pair_mode(const CUtensorMap &a, const CUtensorMap &b0, const 
   p.tail_split = g;
   // No pair without work: at most all tiles' parts.
   if (p.dp_waves == 0 && pairs > left * g) pairs = left * g;
+  p.n_items = p.dp_waves * pairs + left * g;
+  p.dynamic = sched_counter != nullptr ? 1 : 0;
+  p.sched_counter = sched_counter;
   cfg.gridDim = dim3(2 * pairs);
   e = cudaLaunchKernelEx(&cfg, kern, a, b0, b1, p);
   if (e != cudaSuccess) return e;
@@ -391,16 +480,16 @@ cudaError_t launch_pair_mode(const CUtensorMap &a, const CUtensorMap &b0, const 
 int tc2_smem_bytes() { return kStages * kStageBytes + static_cast<int>(sizeof(PairTail)) + 1024; }
 
 cudaError_t tc2_launch(int mode, const CUtensorMap &a, const CUtensorMap &b0, const CUtensorMap &b1, TcParams p,
-                       int max_pairs, int tail_split, cudaStream_t stream) {
+                       int max_pairs, int tail_split, int *sched_counter, cudaStream_t stream) {
   switch (mode) {
     case TC_SWIGLU_BF16:
-      return launch_pair_mode<TC_SWIGLU_BF16>(a, b0, b1, p, max_pairs, tail_split, stream);
+      return launch_pair_mode<TC_SWIGLU_BF16>(a, b0, b1, p, max_pairs, tail_split, sched_counter, stream);
     case TC_SWIGLU_F32:
-      return launch_pair_mode<TC_SWIGLU_F32>(a, b0, b1, p, max_pairs, tail_split, stream);
+      return launch_pair_mode<TC_SWIGLU_F32>(a, b0, b1, p, max_pairs, tail_split, sched_counter, stream);
     case TC_MATMUL_F32:
-      return launch_pair_mode<TC_MATMUL_F32>(a, b0, b1, p, max_pairs, tail_split, stream);
+      return launch_pair_mode<TC_MATMUL_F32>(a, b0, b1, p, max_pairs, tail_split, sched_counter, stream);
     case TC_MATMUL_F32_ACC:
-      return launch_pair_mode<TC_MATMUL_F32_ACC>(a, b0, b1, p, max_pairs, tail_split, stream);
+      return launch_pair_mode<TC_MATMUL_F32_ACC>(a, b0, b1, p, max_pairs, tail_split, sched_counter, stream);
     default:
       return cudaErrorInvalidValue;
   }

@@ -29,6 +29,12 @@ struct TcParams {
   // tail_split narrower tiles (1, 2 or 4) dealt round-robin over the pairs.
   int dp_waves;
   int tail_split;
+  // Dynamic scheduling (dynamic != 0): each pair's leader draws work items
+  // 0 .. n_items-1 (whole tiles, then tail parts) from *sched_counter, a
+  // zeroed device int that the last draw of a launch sets back to zero.
+  int dynamic;
+  int n_items;
+  int *sched_counter;
 };
 
 int tc_smem_bytes();
@@ -36,8 +42,12 @@ int tc_smem_bytes();
 // 2 x min(tiles, co-resident pairs, max_pairs if > 0).  tail_split: 0 =
 // choose, 1/2/4 = cut the leftover tiles into that many column parts.
 int tc2_smem_bytes();
+// sched_counter: a zeroed device int for the dynamic scheduler, or nullptr
+// for the static round-robin schedule.
 cudaError_t tc2_launch(int mode, const CUtensorMap &a, const CUtensorMap &b0, const CUtensorMap &b1,
-                       TcParams p, int max_pairs, int tail_split, cudaStream_t stream);
+                       TcParams p, int max_pairs, int tail_split, int *sched_counter, cudaStream_t stream);
+// Device bytes the dynamic scheduler needs (one zeroed int).
+constexpr size_t kTc2SchedBytes = 256;
 int tc_threads();
 int tc_tile_n(int mode);
 cudaError_t tc_launch(int mode, const CUtensorMap &a, const CUtensorMap &b0, const CUtensorMap &b1,

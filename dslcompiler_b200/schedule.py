@@ -25,7 +25,7 @@ from . import capi
 
 TARGET = "b200-sm100a"
 DEFAULT_DB = os.path.join(os.path.dirname(os.path.abspath(__file__)), "schedules", "schedule_db.json")
-PLAN_FIELDS = ("variant", "block_m", "block_n", "block_k", "stages", "split_k", "grid", "threads", "smem_bytes")
+PLAN_FIELDS = ("variant", "block_m", "block_n", "block_k", "stages", "split_k", "grid", "threads", "smem_bytes", "sched")
 VARIANT_NAMES = {v: k for k, v in capi.VARIANTS.items()}
 OPS = {"fused_swiglu": capi.LLK_OP_FUSED_SWIGLU, "matmul": capi.LLK_OP_MATMUL}
 DTYPES = {"bf16": capi.LLK_DTYPE_BF16, "f32": capi.LLK_DTYPE_FP32}

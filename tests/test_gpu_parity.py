@@ -370,15 +370,16 @@ def test_cta_pair_and_single_cta_kernels_agree(M, K, N, op):
     llk.synchronize(0)
     assert rel_err(host(y_pair), ref) < 1e-5
     # leftover tiles cut into 1, 2 or 4 column parts (MMA N 256 / 128 / 64)
-    for split in (1, 2, 4):
-        key.insert_plan(**dict(base, split_k=split, grid=2 * 7))  # 7 pairs: every shape leaves a tail
+    for split, sched in ((1, 0), (2, 0), (4, 0), (0, 1), (4, 1)):
+        # 7 pairs: every shape leaves a tail; sched 0 = dynamic, 1 = static
+        key.insert_plan(**dict(base, split_k=split, grid=2 * 7, sched=sched))
         try:
             y_split = run()
             torch.cuda.synchronize()
             llk.synchronize(0)
         finally:
             key.insert_plan(**base)
-        assert torch.equal(y_split, y_pair), split  # same per-element accumulation order
+        assert torch.equal(y_split, y_pair), (split, sched)  # same per-element accumulation order
     single = dict(base, block_m=128, grid=148, stages=4)
     key.insert_plan(**single)
     try:
