@@ -58,6 +58,14 @@ struct DeviceState {
   int *status = nullptr;       // device error word written by the kernels
   DeviceBuffer stage[4];       // host-staging buffers: x, wg, wu, y
   DeviceBuffer workspace;      // split-K partials when the caller gives no scratch
+  // Pipelined host-buffer SwiGLU: double-buffered weight / Y column chunks,
+  // a copy-in and a copy-out stream, and their events.
+  DeviceBuffer chunk_w[2][2];  // [buffer][gate, up]
+  DeviceBuffer chunk_y[2];
+  DeviceBuffer chunk_x[2];
+  cudaStream_t copy_in = nullptr, copy_out = nullptr;
+  cudaEvent_t ev_x = nullptr, ev_in[2] = {nullptr, nullptr}, ev_k[2] = {nullptr, nullptr},
+              ev_out[2] = {nullptr, nullptr};
   std::mutex mu;
 };
 
@@ -461,6 +469,144 @@ int read_and_clear_status(DeviceState &ds, cudaStream_t stream) {
   return LLK_OK;
 }
 
+// The copy streams and events of the pipelined host-buffer paths (once).
+int copy_streams(DeviceState &ds) {
+  if (ds.copy_in) return LLK_OK;
+  if (cudaStreamCreateWithFlags(&ds.copy_in, cudaStreamNonBlocking) != cudaSuccess ||
+      cudaStreamCreateWithFlags(&ds.copy_out, cudaStreamNonBlocking) != cudaSuccess ||
+      cudaEventCreateWithFlags(&ds.ev_x, cudaEventDisableTiming) != cudaSuccess)
+    return LLK_ERR_CUDA;
+  for (int b = 0; b < 2; ++b)
+    if (cudaEventCreateWithFlags(&ds.ev_in[b], cudaEventDisableTiming) != cudaSuccess ||
+        cudaEventCreateWithFlags(&ds.ev_k[b], cudaEventDisableTiming) != cudaSuccess ||
+        cudaEventCreateWithFlags(&ds.ev_out[b], cudaEventDisableTiming) != cudaSuccess)
+      return LLK_ERR_CUDA;
+  return LLK_OK;
+}
+
+// SwiGLU with X and Y in host memory and the weights on the device (packed
+// weights, or device buffers), pipelined over row blocks of X: block b+1
+// travels host->device while block b computes and block b-1's Y travels
+// back.  LLK_ERR_UNSUPPORTED (before doing anything) when it does not suit.
+// Called with ds.mu held.
+int swiglu_rows_pipelined(DeviceState &ds, const Tensor2D *x, const DevTensor &wg, const DevTensor &wu, Tensor2D *y,
+                          int y_f32, int requested, KernelContext *ctx, cudaStream_t stream) {
+  const int64_t M = x->dim0, K = x->dim1, N = wg.cols;
+  constexpr int kBlocks = 4;
+  if (M == 0 || N == 0 || K == 0 || K % 8 != 0 || x->stride1 != 1 || y->stride1 != 1 || x->stride0 < K ||
+      y->stride0 < N)
+    return LLK_ERR_UNSUPPORTED;
+  int64_t rb = (M + kBlocks - 1) / kBlocks;
+  rb = (rb + 255) / 256 * 256;  // whole 256-row CTA-pair tiles per block
+  if (rb >= M) return LLK_ERR_UNSUPPORTED;
+  const int yel = y_f32 ? 4 : 2;
+  if (copy_streams(ds) != LLK_OK) return LLK_ERR_CUDA;
+  for (int b = 0; b < 2; ++b)
+    if (ds.chunk_x[b].ensure(static_cast<size_t>(rb) * K * 2) != cudaSuccess ||
+        ds.chunk_y[b].ensure(static_cast<size_t>(rb) * N * yel) != cudaSuccess)
+      return LLK_ERR_NOMEM;
+  if (cudaEventRecord(ds.ev_x, stream) != cudaSuccess || cudaStreamWaitEvent(ds.copy_in, ds.ev_x, 0) ||
+      cudaStreamWaitEvent(ds.copy_out, ds.ev_x, 0))
+    return LLK_ERR_CUDA;
+  int blk = 0;
+  for (int64_t r0 = 0; r0 < M; r0 += rb, ++blk) {
+    const int b = blk & 1;
+    const int64_t h = (M - r0) < rb ? (M - r0) : rb;
+    if (blk >= 2 && (cudaStreamWaitEvent(ds.copy_in, ds.ev_k[b], 0) != cudaSuccess ||
+                     cudaStreamWaitEvent(stream, ds.ev_out[b], 0) != cudaSuccess))
+      return LLK_ERR_CUDA;
+    if (cudaMemcpy2DAsync(ds.chunk_x[b].ptr, K * 2, static_cast<const char *>(x->data) + r0 * x->stride0 * 2,
+                          x->stride0 * 2, K * 2, h, cudaMemcpyHostToDevice, ds.copy_in) != cudaSuccess ||
+        cudaEventRecord(ds.ev_in[b], ds.copy_in) != cudaSuccess ||
+        cudaStreamWaitEvent(stream, ds.ev_in[b], 0) != cudaSuccess)
+      return LLK_ERR_CUDA;
+    const DevTensor dx = {ds.chunk_x[b].ptr, h, K, K, 1};
+    const DevTensor dy = {ds.chunk_y[b].ptr, h, N, N, 1};
+    int rc = launch_device(ds, LLK_OP_FUSED_SWIGLU, dx, wg, wu, dy, y_f32, 0, requested, ctx ? ctx->scratch : nullptr,
+                           ctx ? ctx->scratch_size : 0, stream);
+    if (rc != LLK_OK) return rc;
+    if (cudaEventRecord(ds.ev_k[b], stream) != cudaSuccess ||
+        cudaStreamWaitEvent(ds.copy_out, ds.ev_k[b], 0) != cudaSuccess ||
+        cudaMemcpy2DAsync(static_cast<char *>(y->data) + r0 * y->stride0 * yel, y->stride0 * yel, ds.chunk_y[b].ptr,
+                          N * yel, N * yel, h, cudaMemcpyDeviceToHost, ds.copy_out) != cudaSuccess ||
+        cudaEventRecord(ds.ev_out[b], ds.copy_out) != cudaSuccess)
+      return LLK_ERR_CUDA;
+  }
+  if (cudaStreamWaitEvent(stream, ds.ev_out[(blk - 1) & 1], 0) != cudaSuccess) return LLK_ERR_CUDA;
+  if (cudaStreamSynchronize(ds.copy_out) != cudaSuccess) return LLK_ERR_CUDA;
+  return read_and_clear_status(ds, stream);
+}
+
+// SwiGLU with X, Wg, Wu and Y all in host memory, pipelined over column
+// chunks of N: the weights of chunk c+1 travel host->device on one stream
+// while chunk c computes, and Y of chunk c travels back on another -- so a
+// call costs about the weight transfer instead of transfer + compute +
+// transfer.  Falls back (returns LLK_ERR_UNSUPPORTED before doing anything)
+// when the shape does not suit.  Called with ds.mu held.
+int swiglu_host_pipelined(DeviceState &ds, const Tensor2D *x, const Tensor2D *wg, const Tensor2D *wu, Tensor2D *y,
+                          int y_f32, int requested, KernelContext *ctx, cudaStream_t stream) {
+  const int64_t M = x->dim0, K = x->dim1, N = wg->dim1;
+  constexpr int kChunks = 8;
+  if (M == 0 || N == 0 || K == 0 || K % 8 != 0) return LLK_ERR_UNSUPPORTED;
+  if (x->stride1 != 1 || wg->stride1 != 1 || wu->stride1 != 1 || y->stride1 != 1) return LLK_ERR_UNSUPPORTED;
+  if (x->stride0 < K || wg->stride0 < N || wu->stride0 < N || y->stride0 < N) return LLK_ERR_UNSUPPORTED;
+  int64_t cw = (N + kChunks - 1) / kChunks;
+  cw = (cw + 127) / 128 * 128;  // whole 128-column tiles per chunk
+  if (cw >= N) return LLK_ERR_UNSUPPORTED;  // too narrow to pipeline
+  const int yel = y_f32 ? 4 : 2;
+  if (copy_streams(ds) != LLK_OK) return LLK_ERR_CUDA;
+  const size_t xbytes = static_cast<size_t>(M) * K * 2;
+  if (ds.stage[0].ensure(xbytes) != cudaSuccess) return LLK_ERR_NOMEM;
+  for (int b = 0; b < 2; ++b) {
+    if (ds.chunk_w[b][0].ensure(static_cast<size_t>(K) * cw * 2) != cudaSuccess ||
+        ds.chunk_w[b][1].ensure(static_cast<size_t>(K) * cw * 2) != cudaSuccess ||
+        ds.chunk_y[b].ensure(static_cast<size_t>(M) * cw * yel) != cudaSuccess)
+      return LLK_ERR_NOMEM;
+  }
+  // The caller's stream is the compute stream; the copy streams start after
+  // whatever the caller queued before this call.
+  if (cudaEventRecord(ds.ev_k[0], stream) != cudaSuccess || cudaStreamWaitEvent(ds.copy_in, ds.ev_k[0], 0) ||
+      cudaStreamWaitEvent(ds.copy_out, ds.ev_k[0], 0))
+    return LLK_ERR_CUDA;
+  if (cudaMemcpy2DAsync(ds.stage[0].ptr, K * 2, x->data, x->stride0 * 2, K * 2, M, cudaMemcpyHostToDevice,
+                        ds.copy_in) != cudaSuccess ||
+      cudaEventRecord(ds.ev_x, ds.copy_in) != cudaSuccess || cudaStreamWaitEvent(stream, ds.ev_x, 0) != cudaSuccess)
+    return LLK_ERR_CUDA;
+  const DevTensor dx = {ds.stage[0].ptr, M, K, K, 1};
+  int chunk = 0;
+  for (int64_t c0 = 0; c0 < N; c0 += cw, ++chunk) {
+    const int b = chunk & 1;
+    const int64_t w = (N - c0) < cw ? (N - c0) : cw;
+    // buffer b was last read by chunk-2's kernel and written to host by its D2H
+    if (chunk >= 2 && (cudaStreamWaitEvent(ds.copy_in, ds.ev_k[b], 0) != cudaSuccess ||
+                       cudaStreamWaitEvent(stream, ds.ev_out[b], 0) != cudaSuccess))
+      return LLK_ERR_CUDA;
+    const Tensor2D *ws[2] = {wg, wu};
+    for (int m = 0; m < 2; ++m)
+      if (cudaMemcpy2DAsync(ds.chunk_w[b][m].ptr, cw * 2, static_cast<const char *>(ws[m]->data) + c0 * 2,
+                            ws[m]->stride0 * 2, w * 2, K, cudaMemcpyHostToDevice, ds.copy_in) != cudaSuccess)
+        return LLK_ERR_CUDA;
+    if (cudaEventRecord(ds.ev_in[b], ds.copy_in) != cudaSuccess ||
+        cudaStreamWaitEvent(stream, ds.ev_in[b], 0) != cudaSuccess)
+      return LLK_ERR_CUDA;
+    const DevTensor dg = {ds.chunk_w[b][0].ptr, K, w, cw, 1}, du = {ds.chunk_w[b][1].ptr, K, w, cw, 1};
+    const DevTensor dy = {ds.chunk_y[b].ptr, M, w, cw, 1};
+    int rc = launch_device(ds, LLK_OP_FUSED_SWIGLU, dx, dg, du, dy, y_f32, 0, requested,
+                           ctx ? ctx->scratch : nullptr, ctx ? ctx->scratch_size : 0, stream);
+    if (rc != LLK_OK) return rc;
+    if (cudaEventRecord(ds.ev_k[b], stream) != cudaSuccess ||
+        cudaStreamWaitEvent(ds.copy_out, ds.ev_k[b], 0) != cudaSuccess ||
+        cudaMemcpy2DAsync(static_cast<char *>(y->data) + c0 * yel, y->stride0 * yel, ds.chunk_y[b].ptr, cw * yel,
+                          w * yel, M, cudaMemcpyDeviceToHost, ds.copy_out) != cudaSuccess ||
+        cudaEventRecord(ds.ev_out[b], ds.copy_out) != cudaSuccess)
+      return LLK_ERR_CUDA;
+  }
+  // the call returns with Y on the host; the caller's stream waits for it too
+  if (cudaStreamWaitEvent(stream, ds.ev_out[(chunk - 1) & 1], 0) != cudaSuccess) return LLK_ERR_CUDA;
+  if (cudaStreamSynchronize(ds.copy_out) != cudaSuccess) return LLK_ERR_CUDA;
+  return read_and_clear_status(ds, stream);
+}
+
 // Common body of the SwiGLU / matmul entry points.  wu may equal wg (matmul).
 int run_op(int op, const Tensor2D *x, const Tensor2D *wg, const Tensor2D *wu, Tensor2D *y, int y_f32, int accumulate,
            KernelContext *ctx, const llk_gpu_context *gpu, const DevTensor *packed_g = nullptr,
@@ -479,6 +625,16 @@ int run_op(int op, const Tensor2D *x, const Tensor2D *wg, const Tensor2D *wu, Te
   bool any_host;
   {
     std::lock_guard<std::mutex> lk(ds->mu);
+    if (op == LLK_OP_FUSED_SWIGLU && !packed_g && x->data && wg->data && wu->data && y->data &&
+        !is_device_ptr(x->data) && !is_device_ptr(wg->data) && !is_device_ptr(wu->data) && !is_device_ptr(y->data)) {
+      rc = swiglu_host_pipelined(*ds, x, wg, wu, y, y_f32, requested, ctx, stream);
+      if (rc != LLK_ERR_UNSUPPORTED) return rc;
+    }
+    if (op == LLK_OP_FUSED_SWIGLU && packed_g && x->data && y->data && !is_device_ptr(x->data) &&
+        !is_device_ptr(y->data)) {
+      rc = swiglu_rows_pipelined(*ds, x, *packed_g, *packed_u, y, y_f32, requested, ctx, stream);
+      if (rc != LLK_ERR_UNSUPPORTED) return rc;
+    }
     if ((rc = stage_in(x, 2, ds->stage[0], true, stream, &sx)) != LLK_OK) return rc;
     if (packed_g) {
       sg.t = *packed_g;

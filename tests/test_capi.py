@@ -147,3 +147,29 @@ def test_memref_shim_reports_status():
     m = capi.MemRef2D()
     L.llk_swiglu_memref(None, ctypes.byref(m), ctypes.byref(m), None, ctypes.byref(m))
     assert L.llk_last_status() == capi.LLK_ERR_ARG
+
+
+def _build_c_smoke(tmp_path):
+    exe = tmp_path / "c_abi_smoke"
+    cmd = ["gcc", "-std=c11", "-Wall", "-Werror", "-I", os.path.join(ROOT, "include"),
+           os.path.join(ROOT, "tests", "c_abi_smoke.c"), "-L", os.path.dirname(capi.LIB_PATH), "-lllk_b200",
+           "-Wl,-rpath," + os.path.dirname(capi.LIB_PATH), "-o", str(exe)]
+    import subprocess
+    subprocess.run(cmd, check=True)
+    return exe
+
+
+def test_header_is_c_and_links(tmp_path):
+    import subprocess
+    exe = _build_c_smoke(tmp_path)
+    r = subprocess.run([str(exe)], capture_output=True, text=True, timeout=120)
+    assert r.returncode == 0, r.stdout + r.stderr
+    assert r.stdout.startswith("ok ")
+
+
+@pytest.mark.gpu
+def test_c_program_runs_swiglu_on_gpu(tmp_path):
+    import subprocess
+    exe = _build_c_smoke(tmp_path)
+    r = subprocess.run([str(exe)], capture_output=True, text=True, timeout=120)
+    assert r.returncode == 0 and r.stdout.startswith("ok 0 "), r.stdout + r.stderr

@@ -169,6 +169,32 @@ def test_host_buffers_through_c_abi():
     assert np.array_equal(y, yd.cpu().view(torch.int16).numpy().view(np.uint16))
 
 
+@pytest.mark.parametrize("M,K,N", [(300, 512, 1000), (2048, 256, 11008), (20, 64, 4096)])
+def test_host_buffers_pipelined_chunks_match_device_path(M, K, N):
+    """Host X/Wg/Wu/Y: weights and Y travel in column chunks overlapped with
+    the kernel; the result equals the device-buffer call."""
+    x, wg, wu = dg.swiglu_inputs(M, K, N, 1.0, 0.02, seed=N)
+    y = np.full((M, N + 3), 0xFFFF, np.uint16)[:, :N]  # strided host output
+    st = llk.swiglu_c_abi(x, wg, wu, y)
+    assert st == capi.LLK_OK
+    yd = llk.fused_swiglu(dev(x), dev(wg), dev(wu), variant="tc")
+    torch.cuda.synchronize()
+    assert np.array_equal(y, yd.cpu().view(torch.int16).numpy().view(np.uint16))
+
+
+@pytest.mark.parametrize("M,K,N", [(1000, 512, 640), (2048, 256, 1408)])
+def test_packed_weights_host_rows_pipelined(M, K, N):
+    """Packed (device) weights with host X/Y: row blocks of X travel in,
+    blocks of Y travel out, overlapped with the kernel."""
+    x, wg, wu = dg.swiglu_inputs(M, K, N, 1.0, 0.02, seed=M)
+    pw = llk.PackedWeights(dev(wg), dev(wu))
+    y = pw(x)
+    yd = pw(dev(x))
+    torch.cuda.synchronize()
+    assert np.array_equal(y, yd.cpu().view(torch.int16).numpy().view(np.uint16))
+    pw.close()
+
+
 def test_memref_kernelfn_shim():
     import ctypes
     g = load_golden("small_4_8_16")
