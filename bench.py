@@ -173,6 +173,22 @@ def reference_arm(args):
     return 0
 
 
+class stdout_to_stderr:
+    """Points file descriptor 1 at stderr for the duration (C libraries
+    included)."""
+
+    def __enter__(self):
+        sys.stdout.flush()
+        self.saved = os.dup(1)
+        os.dup2(2, 1)
+        return self
+
+    def __exit__(self, *a):
+        sys.stdout.flush()
+        os.dup2(self.saved, 1)
+        os.close(self.saved)
+
+
 def bf16_tensor(a_u16, pin=False):
     import torch
 
@@ -205,7 +221,12 @@ def our_arm(args):
     rank, local, world = dist_env()
     torch.cuda.set_device(local)
     if world > 1:
-        dist.init_process_group("nccl", device_id=torch.device("cuda", local))
+        # NCCL may print its banner on stdout when the communicator comes up;
+        # keep stdout for the one JSON line.
+        with stdout_to_stderr():
+            dist.init_process_group("nccl", device_id=torch.device("cuda", local))
+            dist.barrier(device_ids=[local])
+            torch.cuda.synchronize()
     dev = torch.device("cuda", local)
     stream = torch.cuda.current_stream(dev)
 

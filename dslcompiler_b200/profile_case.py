@@ -17,11 +17,16 @@ from dslcompiler_b200 import datagen as dg
 
 def main(argv=None) -> int:
     ap = argparse.ArgumentParser()
-    ap.add_argument("config", choices=sorted(dg.CONFIGS))
+    ap.add_argument("config", choices=sorted(dg.CONFIGS) + ["shape"])
+    ap.add_argument("--shape", default=None, help="M,K,N for config 'shape' (SwiGLU, bf16 Y)")
     ap.add_argument("--launches", type=int, default=3)
     ap.add_argument("--variant", default="auto")
     a = ap.parse_args(argv)
-    c = dg.CONFIGS[a.config]
+    if a.config == "shape":
+        M_, K_, N_ = (int(v) for v in a.shape.split(","))
+        c = dict(kind="swiglu", M=M_, K=K_, N=N_, x_std=1.0, w_std=0.02, y="bf16")
+    else:
+        c = dg.CONFIGS[a.config]
     g = torch.Generator(device="cuda").manual_seed(42)
     M, K, N = c["M"], c["K"], c["N"]
     if c["kind"] == "matmul":
