@@ -12,8 +12,9 @@ configured shapes and distributions.
     torchrun --nproc-per-node N bench.py --gpus N ...
 
 value: whole-job TFLOP/s = 4*M*N*K / (max over ranks of the summed
-per-step kernel times / K), inputs resident in HBM, L2 flushed (256 MiB
-read) before every timed step.  e2e: the same metric through the C ABI
+K back-to-back steps, one CUDA event pair), inputs resident in HBM; steps
+cycle through enough distinct input sets that their total exceeds 2x L2, so
+no step finds its inputs in L2.  e2e: the same metric through the C ABI
 ``llk_swiglu`` with pinned HOST buffers (H2D of X, Wg, Wu and D2H of Y in
 the timed region, every step).  --impl reference times the CPU restatement
 of the reference's fused AVX2 schedule on this host's cores instead.
@@ -38,7 +39,6 @@ sys.path.insert(0, ROOT)
 CONFIG = dict(name="c3", M=2048, K=4096, N=11008, x_std=1.0, w_std=0.02)
 METRIC = "fused SwiGLU BF16 TFLOP/s (Llama-7B prefill shape, config 3)"
 UNIT = "TFLOP/s"
-FLUSH_BYTES = 256 << 20
 
 
 def dist_env():
@@ -46,12 +46,16 @@ def dist_env():
 
 
 def measured_peaks():
+    """(bf16 TFLOP/s, HBM GB/s, source).  The bf16 figure is the SUSTAINED
+    one: the timed loop runs back to back for a sizeable fraction of a
+    second, long enough for the 1 kW power cap to set the clock, which is the
+    regime of the seconds-long cuBLAS loop the sustained figure measures."""
     p = os.path.join(ROOT, "MEASURED_PEAKS.json")
     if os.path.exists(p):
         with open(p) as f:
             d = json.load(f)
-        return d.get("bf16_tflops"), d.get("hbm_gbs"), "measured"
-    return 1590.0, 6650.0, "fallback"
+        return d.get("bf16_tflops_sustained") or d.get("bf16_tflops"), d.get("hbm_gbs"), "measured"
+    return 1400.0, 6650.0, "fallback"
 
 
 def profile_traffic(name):
@@ -196,8 +200,35 @@ def bf16_tensor(a_u16, pin=False):
     return t.pin_memory() if pin else t
 
 
+def input_sets(dev, tensors, l2_bytes):
+    """Enough distinct copies of a step's device tensors that together they
+    exceed twice the L2: back-to-back steps cycling through them never find
+    their inputs in L2 from an earlier step."""
+    import torch
+
+    per = sum(t.numel() * t.element_size() for t in tensors)
+    n = max(1, min(16, -(-2 * l2_bytes // per)))
+    sets = [tuple(tensors)] + [tuple(t.clone() for t in tensors) for _ in range(n - 1)]
+    torch.cuda.synchronize(dev)
+    return sets, per
+
+
+def time_back_to_back(fn, steps, stream):
+    """Total CUDA-event time (ms) of `steps` back-to-back calls fn(i)."""
+    import torch
+
+    s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    s.record(stream)
+    for i in range(steps):
+        fn(i)
+    e.record(stream)
+    torch.cuda.synchronize()
+    return s.elapsed_time(e)
+
+
 def time_steps(fn, flush, steps, stream):
-    """Per-step CUDA-event durations (ms) of fn(), L2 flushed before each."""
+    """Per-step CUDA-event durations (ms) of fn() (host-synchronous steps such
+    as the host-buffer e2e calls); flush, if given, runs before each step."""
     import torch
 
     evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(steps)]
@@ -239,17 +270,12 @@ def our_arm(args):
 
     xd, gd, ud = bf16_tensor(x).to(dev), bf16_tensor(wg_s).to(dev), bf16_tensor(wu_s).to(dev)
     yd = torch.empty((M, n_r), dtype=torch.bfloat16, device=dev)
-    flush_buf = torch.empty(FLUSH_BYTES, dtype=torch.uint8, device=dev)
+    l2 = torch.cuda.get_device_properties(dev).L2_cache_size
+    sets, set_bytes = input_sets(dev, [xd, gd, ud, yd], l2)
 
-    flush_view = flush_buf.view(torch.float32)
-
-    def flush():
-        # Read (not write) 256 MiB: evicts the L2 with clean lines, so no
-        # write-back of the flush lands inside the next timed step.
-        flush_view.sum()
-
-    def step():
-        llk.fused_swiglu(xd, gd, ud, out=yd)
+    def step(i):
+        a, b, c, d = sets[i % len(sets)]
+        llk.fused_swiglu(a, b, c, out=d)
 
     def barrier():
         if world > 1:
@@ -270,9 +296,8 @@ def our_arm(args):
         return float(t.item())
 
     # ---------------------------------------------------------- value
-    for _ in range(args.warmup):
-        flush()
-        step()
+    for i in range(args.warmup):
+        step(i)
     torch.cuda.synchronize()
     llk.synchronize(local)
     barrier()
@@ -281,14 +306,13 @@ def our_arm(args):
     if sampler:
         sampler.__enter__()
     t_wall0 = time.perf_counter()
-    times = time_steps(step, flush, args.steps, stream)
+    kernel_ms = time_back_to_back(step, args.steps, stream)
     t_wall = time.perf_counter() - t_wall0
     barrier()
     torch.cuda.synchronize()
     if sampler:
         sampler.__exit__()
     llk.synchronize(local)
-    kernel_ms = sum(times)
     job_ms = max_over_ranks(kernel_ms) / args.steps
     total_flops = 4.0 * M * N * K
     value = total_flops / (job_ms * 1e-3) / 1e12
@@ -345,7 +369,7 @@ def our_arm(args):
         extras["gather_y"] = gather_timing(args, dev, stream, yd, N, world, barrier, max_over_ranks)
     cpu = None
     if world == 1 and not args.quick:
-        extras = single_gpu_extras(args, dev, stream, flush, peak_tf, peak_gbs)
+        extras = single_gpu_extras(args, dev, stream, peak_tf, peak_gbs)
         if not args.no_cpu_baseline:
             cpu = cpu_baseline(x, wg, wu)
 
@@ -358,11 +382,15 @@ def our_arm(args):
             "data": "synthetic (seeded splitmix64/Box-Muller, X~N(0,1), W~N(0,0.02), rounded to bf16)",
             "config": {"workload": "c3 llama7b-prefill swiglu", "M": M, "K": K, "N": N,
                        "parallelism": f"N-column-sharded x{world} (no collective)" if world > 1 else "single GPU",
-                       "shard_cols_rank0": n_r, "l2": "flushed before every timed step (256 MiB read)",
-                       "timing": "CUDA events around each kernel launch, summed, max over ranks"},
+                       "shard_cols_rank0": n_r,
+                       "l2": f"no flush: back-to-back steps cycle {len(sets)} distinct input sets of "
+                             f"{set_bytes / 2**20:.0f} MiB (together >= 2 x the {l2 / 2**20:.0f} MiB L2)",
+                       "timing": "one CUDA event pair around all timed steps (launches back to back), "
+                                 "max over ranks"},
             "roofline": {"bound": "tensor", "achieved": achieved, "peak": peak_tf, "unit": "TFLOP/s",
                          "frac": achieved / peak_tf, "traffic": traffic,
-                         "peak_source": f"{peak_src} bf16 burst (MEASURED_PEAKS.json)",
+                         "peak_source": f"{peak_src} bf16 sustained (MEASURED_PEAKS.json bf16_tflops_sustained): "
+                                        "the timed loop is back to back and power-capped",
                          "kernel": "tc2_kernel<TC_SWIGLU_BF16> (CTA pairs)" if M > 128 else "tc_swiglu_kernel<TC_SWIGLU_BF16>",
                          "algorithmic_work": "4*M*N_rank*K FLOP per launch"},
             "e2e": e2e, "e2e_packed_weights": e2e_packed,
@@ -412,7 +440,7 @@ def gather_timing(args, dev, stream, yd, N, world, barrier, max_over_ranks):
             "what": "all_gather_into_tensor (NCCL) of padded Y shards + llk_gather_columns relayout"}
 
 
-def single_gpu_extras(args, dev, stream, flush, peak_tf, peak_gbs):
+def single_gpu_extras(args, dev, stream, peak_tf, peak_gbs):
     """Secondary measurements on one GPU: the micro.mma matmul (config 2)
     and the decode shapes (config 4) -- same timing rules."""
     import torch
@@ -422,14 +450,19 @@ def single_gpu_extras(args, dev, stream, flush, peak_tf, peak_gbs):
 
     out = {}
     steps = max(5, min(args.steps, 200))
+    l2 = torch.cuda.get_device_properties(dev).L2_cache_size
     a, b = dg.config_inputs("c2")
     ad, bd = bf16_tensor(a).to(dev), bf16_tensor(b).to(dev)
     cd = torch.empty((4096, 4096), dtype=torch.float32, device=dev)
-    fn = lambda: llk.matmul(ad, bd, cd)  # noqa: E731
-    for _ in range(3):
-        fn()
-    t = time_steps(fn, flush, steps, stream)
-    ms = sum(t) / len(t)
+    msets, _ = input_sets(dev, [ad, bd, cd], l2)
+
+    def fn(i):
+        x_, w_, c_ = msets[i % len(msets)]
+        llk.matmul(x_, w_, c_)
+
+    for i in range(3):
+        fn(i)
+    ms = time_back_to_back(fn, steps, stream) / steps
     out["matmul_c2"] = {"tflops": 2.0 * 4096 ** 3 / (ms * 1e-3) / 1e12, "ms": ms,
                         "frac_of_peak": 2.0 * 4096 ** 3 / (ms * 1e-3) / 1e12 / peak_tf}
     del ad, bd, cd
@@ -439,15 +472,19 @@ def single_gpu_extras(args, dev, stream, flush, peak_tf, peak_gbs):
         x, wg, wu = dg.config_inputs(cfg)
         xd, gd, ud = bf16_tensor(x).to(dev), bf16_tensor(wg).to(dev), bf16_tensor(wu).to(dev)
         yd = torch.empty((c["M"], c["N"]), dtype=torch.bfloat16, device=dev)
-        fn = lambda: llk.fused_swiglu(xd, gd, ud, out=yd)  # noqa: E731
-        for _ in range(3):
-            fn()
-        t = time_steps(fn, flush, steps, stream)
-        ms = sum(t) / len(t)
+        dsets, _ = input_sets(dev, [xd, gd, ud, yd], l2)
+
+        def fn(i):
+            a_, b_, c_, d_ = dsets[i % len(dsets)]
+            llk.fused_swiglu(a_, b_, c_, out=d_)
+
+        for i in range(3):
+            fn(i)
+        ms = time_back_to_back(fn, steps, stream) / steps
         byts = 2 * c["M"] * c["K"] + 4 * c["K"] * c["N"] + 2 * c["M"] * c["N"]
         dec[cfg] = {"us": ms * 1e3, "GB/s": byts / (ms * 1e-3) / 1e9, "frac_of_hbm": byts / (ms * 1e-3) / 1e9 / peak_gbs,
                     "tflops": 4.0 * c["M"] * c["N"] * c["K"] / (ms * 1e-3) / 1e12}
-        del xd, gd, ud, yd
+        del xd, gd, ud, yd, dsets
     out["decode_c4"] = dec
     torch.cuda.synchronize()
     llk.synchronize(dev.index)

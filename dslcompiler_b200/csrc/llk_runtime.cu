@@ -86,6 +86,13 @@ int resolve_device(const llk_gpu_context *gpu, int *dev_out) {
 
 // Makes `dev` current and initialises its state once.
 int device_init(int dev, DeviceState **out) {
+  if (dev >= 0 && dev < kMaxDevices && g_dev[dev].ready) {  // fast path: no driver queries
+    int cur = -1;
+    if (cudaGetDevice(&cur) != cudaSuccess || (cur != dev && cudaSetDevice(dev) != cudaSuccess))
+      return LLK_ERR_DEVICE;
+    *out = &g_dev[dev];
+    return LLK_OK;
+  }
   int count = 0;
   if (cudaGetDeviceCount(&count) != cudaSuccess || count <= 0) {
     cudaGetLastError();
@@ -430,10 +437,12 @@ struct Staged {
   const Tensor2D *src = nullptr;
 };
 
-int stage_in(const Tensor2D *src, int elem, DeviceBuffer &buf, bool copy, cudaStream_t stream, Staged *out) {
+// on_dev: whether src->data is device memory (queried once by the caller).
+int stage_in(const Tensor2D *src, bool on_dev, int elem, DeviceBuffer &buf, bool copy, cudaStream_t stream,
+             Staged *out) {
   out->src = src;
   out->t = {src->data, src->dim0, src->dim1, src->stride0, src->stride1};
-  if (src->dim0 == 0 || src->dim1 == 0 || is_device_ptr(src->data)) return LLK_OK;
+  if (src->dim0 == 0 || src->dim1 == 0 || on_dev) return LLK_OK;
   if (src->stride1 != 1 || src->stride0 < src->dim1) return LLK_ERR_ALIGN;
   out->host = true;
   const size_t pitch = static_cast<size_t>(src->dim1) * elem;
@@ -624,29 +633,32 @@ int run_op(int op, const Tensor2D *x, const Tensor2D *wg, const Tensor2D *wu, Te
   Staged sx, sg, su, sy;
   bool any_host;
   {
+    // Where each buffer lives, asked once per call.
+    const bool dx = is_device_ptr(x->data), dy = is_device_ptr(y->data);
+    const bool dg = packed_g ? true : is_device_ptr(wg->data);
+    const bool du = packed_g ? true : (wu == wg ? dg : is_device_ptr(wu->data));
     std::lock_guard<std::mutex> lk(ds->mu);
-    if (op == LLK_OP_FUSED_SWIGLU && !packed_g && x->data && wg->data && wu->data && y->data &&
-        !is_device_ptr(x->data) && !is_device_ptr(wg->data) && !is_device_ptr(wu->data) && !is_device_ptr(y->data)) {
+    if (op == LLK_OP_FUSED_SWIGLU && !packed_g && x->data && wg->data && wu->data && y->data && !dx && !dg && !du &&
+        !dy) {
       rc = swiglu_host_pipelined(*ds, x, wg, wu, y, y_f32, requested, ctx, stream);
       if (rc != LLK_ERR_UNSUPPORTED) return rc;
     }
-    if (op == LLK_OP_FUSED_SWIGLU && packed_g && x->data && y->data && !is_device_ptr(x->data) &&
-        !is_device_ptr(y->data)) {
+    if (op == LLK_OP_FUSED_SWIGLU && packed_g && x->data && y->data && !dx && !dy) {
       rc = swiglu_rows_pipelined(*ds, x, *packed_g, *packed_u, y, y_f32, requested, ctx, stream);
       if (rc != LLK_ERR_UNSUPPORTED) return rc;
     }
-    if ((rc = stage_in(x, 2, ds->stage[0], true, stream, &sx)) != LLK_OK) return rc;
+    if ((rc = stage_in(x, dx, 2, ds->stage[0], true, stream, &sx)) != LLK_OK) return rc;
     if (packed_g) {
       sg.t = *packed_g;
       su.t = *packed_u;
-    } else if ((rc = stage_in(wg, 2, ds->stage[1], true, stream, &sg)) != LLK_OK) {
+    } else if ((rc = stage_in(wg, dg, 2, ds->stage[1], true, stream, &sg)) != LLK_OK) {
       return rc;
     } else if (wu != wg) {
-      if ((rc = stage_in(wu, 2, ds->stage[2], true, stream, &su)) != LLK_OK) return rc;
+      if ((rc = stage_in(wu, du, 2, ds->stage[2], true, stream, &su)) != LLK_OK) return rc;
     } else {
       su = sg;
     }
-    if ((rc = stage_in(y, yel, ds->stage[3], accumulate != 0, stream, &sy)) != LLK_OK) return rc;
+    if ((rc = stage_in(y, dy, yel, ds->stage[3], accumulate != 0, stream, &sy)) != LLK_OK) return rc;
     any_host = sx.host || sg.host || su.host || sy.host;
     rc = launch_device(*ds, op, sx.t, sg.t, su.t, sy.t, y_f32, accumulate, requested, ctx ? ctx->scratch : nullptr,
                        ctx ? ctx->scratch_size : 0, stream);

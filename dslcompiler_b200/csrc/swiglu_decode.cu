@@ -24,6 +24,7 @@
 #include <cuda.h>
 #include <cuda_runtime.h>
 
+#include <atomic>
 #include <cstdint>
 
 #include "decode_kernels.h"
@@ -430,8 +431,17 @@ cudaError_t decode_launch(const CUtensorMap &wg, const CUtensorMap &wu, const CU
   p.partials = reinterpret_cast<float *>(static_cast<char *>(workspace) + kCounterRegion);
   p.status = status;
   const int smem = d.stages * stage_bytes_for(d.block_m) + static_cast<int>(sizeof(DecodeTail)) + 1024;
-  cudaError_t e = cudaFuncSetAttribute(decode_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
-  if (e != cudaSuccess) return e;
+  // The attribute is set once per device to the most any plan may use.
+  static std::atomic<uint64_t> attr_set{0};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  const uint64_t bit = 1ull << (dev & 63);
+  if (!(attr_set.load(std::memory_order_relaxed) & bit)) {
+    cudaError_t e = cudaFuncSetAttribute(decode_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
+    if (e != cudaSuccess) return e;
+    attr_set.fetch_or(bit);
+  }
+  if (smem > 227 * 1024) return cudaErrorInvalidValue;
   decode_kernel<<<d.grid, kThreads, smem, stream>>>(wg, wu, x, p);
   return cudaGetLastError();
 }

@@ -24,6 +24,7 @@
 #include <cuda.h>
 #include <cuda_runtime.h>
 
+#include <atomic>
 #include <cstdint>
 
 #include "sm100_ptx.cuh"
@@ -310,8 +311,15 @@ static cudaError_t launch_mode(const CUtensorMap &a, const CUtensorMap &b0, cons
                                int grid, cudaStream_t stream) {
   auto kern = tc_swiglu_kernel<MODE>;
   const int smem = tc_smem_bytes();
-  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
-  if (e != cudaSuccess) return e;
+  static std::atomic<uint64_t> attr_set{0};  // bit per device: smem attribute done
+  int dev = 0;
+  cudaGetDevice(&dev);
+  const uint64_t bit = 1ull << (dev & 63);
+  if (!(attr_set.load(std::memory_order_relaxed) & bit)) {
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    if (e != cudaSuccess) return e;
+    attr_set.fetch_or(bit);
+  }
   kern<<<grid, kThreads, smem, stream>>>(a, b0, b1, p);
   return cudaGetLastError();
 }

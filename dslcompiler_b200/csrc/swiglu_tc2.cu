@@ -34,6 +34,7 @@
 #include <cuda.h>
 #include <cuda_runtime.h>
 
+#include <atomic>
 #include <cstdint>
 
 #include "sm100_ptx.cuh"
@@ -418,13 +419,45 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (threadIdx.x == 0 && st->abort != 0 && p.status != nullptr) atomicExch(p.status, st->abort);
 }
 
+// Per device: the smem attribute was set and how many pairs can be resident
+// (a cluster occupancy query costs far more than a launch, so it runs once).
+template <int MODE>
+int resident_pairs() {
+  constexpr int kDevs = 64;
+  static std::atomic<int> cache[kDevs];
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kDevs) return -1;
+  const int c = cache[dev].load(std::memory_order_relaxed);
+  if (c > 0) return c;
+  auto kern = tc2_kernel<MODE>;
+  if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, tc2_smem_bytes()) != cudaSuccess)
+    return -1;
+  cudaLaunchConfig_t cfg = {};
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 2;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.gridDim = dim3(2);
+  cfg.blockDim = dim3(kThreads);
+  cfg.dynamicSmemBytes = tc2_smem_bytes();
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  int clusters = 0;
+  if (cudaOccupancyMaxActiveClusters(&clusters, kern, &cfg) != cudaSuccess || clusters < 1) {
+    cudaGetLastError();
+    clusters = 1;
+  }
+  cache[dev].store(clusters, std::memory_order_relaxed);
+  return clusters;
+}
+
 template <int MODE>
 cudaError_t launch_pair_mode(const CUtensorMap &a, const CUtensorMap &b0, const CUtensorMap &b1, TcParams p,
                              int max_pairs, int tail_split, int *sched_counter, cudaStream_t stream) {
   auto kern = tc2_kernel<MODE>;
-  const int smem = tc2_smem_bytes();
-  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
-  if (e != cudaSuccess) return e;
+  const int clusters = resident_pairs<MODE>();
+  if (clusters < 1) return cudaErrorInvalidValue;
   cudaLaunchConfig_t cfg = {};
   cudaLaunchAttribute attr[1];
   attr[0].id = cudaLaunchAttributeClusterDimension;
@@ -432,17 +465,11 @@ cudaError_t launch_pair_mode(const CUtensorMap &a, const CUtensorMap &b0, const 
   attr[0].val.clusterDim.y = 1;
   attr[0].val.clusterDim.z = 1;
   cfg.blockDim = dim3(kThreads);
-  cfg.dynamicSmemBytes = smem;
+  cfg.dynamicSmemBytes = tc2_smem_bytes();
   cfg.stream = stream;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  cfg.gridDim = dim3(2);
-  int clusters = 0;
-  e = cudaOccupancyMaxActiveClusters(&clusters, kern, &cfg);
-  if (e != cudaSuccess || clusters < 1) {
-    cudaGetLastError();
-    clusters = 1;
-  }
+  cudaError_t e = cudaSuccess;
   int pairs = clusters;
   if (max_pairs >= 1 && pairs > max_pairs) pairs = max_pairs;
   // Whole-tile waves, then the leftover tiles cut into g column parts: the
