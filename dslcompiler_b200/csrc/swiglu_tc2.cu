@@ -25,10 +25,11 @@
 //   warps 2-5  epilogue in both CTAs on their own TMEM rows; each thread
 //              releases the accumulator by arriving on the leader's barrier.
 // Work split: floor(tiles / pairs) waves of whole tiles, one pair per tile;
-// the tiles left over would run as a partly idle last wave, so they are cut
-// along N into 2 or 4 narrower tiles (MMA N = 128 or 64) dealt round-robin
-// over all pairs -- the split that makes the last wave shortest.  No partial
-// sums, no fix-up: every output is still written once from TMEM.
+// the tiles left over would run as a partly idle last wave, so they may be
+// cut along N into 2 or 4 narrower tiles (MMA N = 128 or 64) dealt
+// round-robin over all pairs -- whichever split makes the last wave shortest
+// under the measured cost of a part.  No partial sums, no fix-up: every
+// output is still written once from TMEM.
 //
 // All waits bounded; no TMA multicast (each CTA loads its own tiles).
 #include <cuda.h>
@@ -472,8 +473,12 @@ cudaError_t launch_pair_mode(const CUtensorMap &a, const CUtensorMap &b0, const 
   cudaError_t e = cudaSuccess;
   int pairs = clusters;
   if (max_pairs >= 1 && pairs > max_pairs) pairs = max_pairs;
-  // Whole-tile waves, then the leftover tiles cut into g column parts: the
-  // last wave takes ceil(left * g / pairs) / g tile-times; pick the g that
+  // Whole-tile waves, then the leftover tiles cut into g column parts.  A
+  // part still loads its tile's whole X block (16 KB per CTA per k-block)
+  // but only 1/g of the weight bytes (16 KB / g), and the k-loop is bound by
+  // these L2->shared-memory bytes (measured: a quarter part takes ~0.63 of a
+  // whole tile), so a part costs (1 + 1/g) / 2 tile-times.  The last wave
+  // then takes ceil(left * g / pairs) * (1 + 1/g) / 2; pick the g that
   // makes it shortest (ties: the wider tiles).
   p.dp_waves = p.num_tiles / pairs;
   const int left = p.num_tiles - p.dp_waves * pairs;
@@ -483,7 +488,7 @@ cudaError_t launch_pair_mode(const CUtensorMap &a, const CUtensorMap &b0, const 
   } else if (left > 0) {
     double best = 1e30;
     for (int cand = 1; cand <= 4; cand *= 2) {
-      const double t = static_cast<double>((left * cand + pairs - 1) / pairs) / cand;
+      const double t = static_cast<double>((left * cand + pairs - 1) / pairs) * (1.0 + 1.0 / cand) / 2.0;
       if (t < best - 1e-9) {
         best = t;
         g = cand;
