@@ -368,10 +368,14 @@ def our_arm(args):
     if world > 1:
         extras["gather_y"] = gather_timing(args, dev, stream, yd, N, world, barrier, max_over_ranks)
     cpu = None
-    if world == 1 and not args.quick:
-        extras = single_gpu_extras(args, dev, stream, peak_tf, peak_gbs)
-        if not args.no_cpu_baseline:
-            cpu = cpu_baseline(x, wg, wu)
+    if not args.quick:
+        del sets, xd, gd, ud, yd
+        torch.cuda.empty_cache()
+        extras.update(sharded_extras(args, dev, stream, rank, world, peak_tf, peak_gbs, barrier, max_over_ranks))
+        if world == 1:
+            extras.update(single_gpu_extras(args, dev, stream, peak_tf, peak_gbs))
+            if not args.no_cpu_baseline:
+                cpu = cpu_baseline(x, wg, wu)
 
     clocks = sampler.summary() if sampler else None
     if rank == 0:
@@ -441,8 +445,8 @@ def gather_timing(args, dev, stream, yd, N, world, barrier, max_over_ranks):
 
 
 def single_gpu_extras(args, dev, stream, peak_tf, peak_gbs):
-    """Secondary measurements on one GPU: the micro.mma matmul (config 2)
-    and the decode shapes (config 4) -- same timing rules."""
+    """Secondary measurement on one GPU: the micro.mma matmul (config 2),
+    same timing rules."""
     import torch
 
     import dslcompiler_b200 as llk
@@ -465,29 +469,74 @@ def single_gpu_extras(args, dev, stream, peak_tf, peak_gbs):
     ms = time_back_to_back(fn, steps, stream) / steps
     out["matmul_c2"] = {"tflops": 2.0 * 4096 ** 3 / (ms * 1e-3) / 1e12, "ms": ms,
                         "frac_of_peak": 2.0 * 4096 ** 3 / (ms * 1e-3) / 1e12 / peak_tf}
-    del ad, bd, cd
-    dec = {}
-    for cfg in ("c4_m1", "c4_m4", "c4_m16"):
+    del ad, bd, cd, msets
+    torch.cuda.synchronize()
+    llk.synchronize(dev.index)
+    return out
+
+
+def device_normal_bf16(shape, std, seed, dev):
+    """Seeded N(0, std) bf16 tensor drawn on the device (torch's Philox
+    generator): the multi-GB secondary configurations would take minutes to
+    draw on the host."""
+    import torch
+
+    g = torch.Generator(device=dev)
+    g.manual_seed(seed)
+    return (torch.randn(shape, generator=g, device=dev, dtype=torch.float32) * std).to(torch.bfloat16)
+
+
+def sharded_extras(args, dev, stream, rank, world, peak_tf, peak_gbs, barrier, max_over_ranks):
+    """Secondary configurations at every GPU count, column-sharded like the
+    headline (rank r computes its llk_shard_columns share, no collective):
+    config 5 (Llama-70B prefill SwiGLU, 7.7 TFLOP) and the config-4 decode
+    shapes.  Whole-job figures from the max over ranks of back-to-back
+    CUDA-event time, inputs rotating over sets larger than 2x L2."""
+    import torch
+
+    import dslcompiler_b200 as llk
+    from dslcompiler_b200 import datagen as dg
+
+    out = {}
+    l2 = torch.cuda.get_device_properties(dev).L2_cache_size
+
+    def run(cfg, steps, seed):
         c = dg.CONFIGS[cfg]
-        x, wg, wu = dg.config_inputs(cfg)
-        xd, gd, ud = bf16_tensor(x).to(dev), bf16_tensor(wg).to(dev), bf16_tensor(wu).to(dev)
-        yd = torch.empty((c["M"], c["N"]), dtype=torch.bfloat16, device=dev)
-        dsets, _ = input_sets(dev, [xd, gd, ud, yd], l2)
+        M, K, N = c["M"], c["K"], c["N"]
+        b, e = llk.shard_columns(N, world, rank)
+        xd = device_normal_bf16((M, K), c["x_std"], seed, dev)
+        gd = device_normal_bf16((K, e - b), c["w_std"], seed * 1000 + 2 * rank + 1, dev)
+        ud = device_normal_bf16((K, e - b), c["w_std"], seed * 1000 + 2 * rank + 2, dev)
+        yd = torch.empty((M, e - b), dtype=torch.bfloat16, device=dev)
+        sets, _ = input_sets(dev, [xd, gd, ud, yd], l2)
 
         def fn(i):
-            a_, b_, c_, d_ = dsets[i % len(dsets)]
+            a_, b_, c_, d_ = sets[i % len(sets)]
             llk.fused_swiglu(a_, b_, c_, out=d_)
 
         for i in range(3):
             fn(i)
-        ms = time_back_to_back(fn, steps, stream) / steps
-        byts = 2 * c["M"] * c["K"] + 4 * c["K"] * c["N"] + 2 * c["M"] * c["N"]
-        dec[cfg] = {"us": ms * 1e3, "GB/s": byts / (ms * 1e-3) / 1e9, "frac_of_hbm": byts / (ms * 1e-3) / 1e9 / peak_gbs,
-                    "tflops": 4.0 * c["M"] * c["N"] * c["K"] / (ms * 1e-3) / 1e12}
-        del xd, gd, ud, yd, dsets
+        torch.cuda.synchronize()
+        barrier()
+        ms = max_over_ranks(time_back_to_back(fn, steps, stream)) / steps
+        llk.synchronize(dev.index)
+        del sets, xd, gd, ud, yd
+        torch.cuda.empty_cache()
+        return M, K, N, ms
+
+    M, K, N, ms = run("c5", max(5, min(args.steps, 40)), 55)
+    tf = 4.0 * M * N * K / (ms * 1e-3) / 1e12
+    out["swiglu_c5"] = {"workload": "c5 llama70b-prefill swiglu X[8192,8192] W[8192,28672] bf16",
+                        "tflops": tf, "ms": ms, "frac_of_peak_per_gpu": tf / world / peak_tf,
+                        "data": "synthetic, drawn on the device (torch Philox, seeded), X~N(0,1), W~N(0,0.015)"}
+    dec = {}
+    for i, cfg in enumerate(("c4_m1", "c4_m4", "c4_m16")):
+        M, K, N, ms = run(cfg, max(5, min(args.steps, 200)), 41 + i)
+        byts = 2 * M * K + 4 * K * N + 2 * M * N
+        dec[cfg] = {"us": ms * 1e3, "GB/s": byts / (ms * 1e-3) / 1e9,
+                    "frac_of_hbm_per_gpu": byts / (ms * 1e-3) / 1e9 / world / peak_gbs,
+                    "tflops": 4.0 * M * N * K / (ms * 1e-3) / 1e12}
     out["decode_c4"] = dec
-    torch.cuda.synchronize()
-    llk.synchronize(dev.index)
     return out
 
 

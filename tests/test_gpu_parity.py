@@ -283,6 +283,50 @@ def test_config3_sampled_fp64_and_torch():
     assert not torch.isnan(y).any()
 
 
+def _device_normal_bf16(shape, std, seed):
+    g = torch.Generator(device="cuda")
+    g.manual_seed(seed)
+    return (torch.randn(shape, generator=g, device="cuda", dtype=torch.float32) * std).to(torch.bfloat16)
+
+
+def _bits(t):
+    return t.cpu().view(torch.int16).numpy().view(np.uint16)
+
+
+def test_config5_sampled_fp64_rows_and_torch():
+    """Config 5 (X[8192,8192], Wg/Wu[8192,28672], Y bf16; 1.6 GB of inputs,
+    drawn on the device): 4096 random points plus two whole rows in FP64, 16
+    whole rows against the fused f32 port, and the full tensor against an
+    fp32 torch restatement, column block by column block."""
+    M, K, N = 8192, 8192, 28672
+    xd = _device_normal_bf16((M, K), 1.0, 501)
+    gd = _device_normal_bf16((K, N), 0.015, 502)
+    ud = _device_normal_bf16((K, N), 0.015, 503)
+    y = llk.fused_swiglu(xd, gd, ud)
+    torch.cuda.synchronize()
+    llk.synchronize(0)
+    assert not torch.isnan(y).any()
+    x, wg, wu = _bits(xd), _bits(gd), _bits(ud)
+    yy = host(y)
+    rng = np.random.default_rng(5)
+    rows = np.concatenate([rng.integers(0, M, 4096), np.full(N, 0), np.full(N, M - 1)])
+    cols = np.concatenate([rng.integers(0, N, 4096), np.arange(N), np.arange(N)])
+    ref = oracle.swiglu_fp64_points(x, wg, wu, rows, cols)
+    assert float(np.abs(yy[rows, cols] - ref).max() / np.abs(ref).max()) <= TOL_BF16
+    sample = np.sort(rng.choice(M, 16, replace=False))
+    pref = oracle.port_swiglu(x[sample], wg, wu, "f32").astype(np.float64)
+    assert rel_err(yy[sample], pref) <= TOL_BF16
+    terr, tmax = 0.0, 0.0
+    xf = xd.float()
+    for c0 in range(0, N, 4096):
+        g = xf @ gd[:, c0:c0 + 4096].float()
+        u = xf @ ud[:, c0:c0 + 4096].float()
+        t = g / (1 + torch.exp(-g)) * u
+        terr = max(terr, float((y[:, c0:c0 + 4096].float() - t).abs().max()))
+        tmax = max(tmax, float(t.abs().max()))
+    assert terr / tmax <= TOL_BF16
+
+
 @pytest.mark.parametrize("cfg", ["c4_m1", "c4_m4", "c4_m16"])
 @pytest.mark.parametrize("variant", ["auto", "tc"])
 def test_config4_decode_shapes(cfg, variant):
