@@ -226,10 +226,14 @@ llk_launch_plan build_plan(int variant, int op, int64_t M, int64_t N, int64_t K,
     p.block_k = 64;
     p.stages = pair ? 6 : 4;
     p.split_k = pair ? 0 : 1;  // pair kernel: 0 = choose the tail split
-    // Static round-robin tiles: measured 3-5 % faster than the dynamic work
-    // counter (interleaved A/B on configs 2 and 3 and on 8-GPU shards).
-    p.sched = 1;
     const int64_t tiles = ((M + p.block_m - 1) / p.block_m) * ((N + p.block_n - 1) / p.block_n);
+    // Static round-robin below 12 waves of tiles, the launch-wide work
+    // counter from there on.  Measured on B200 in interleaved A/B: static is
+    // 2-6 % faster for 3-9 waves (configs 2 and 3, 8-GPU shards); over many
+    // waves static pairs drift apart, so the pairs sharing a weight tile no
+    // longer read it from L2 together (M = K = 8192, N = 28672, 97 waves:
+    // 4.8 GB of DRAM reads with the counter, 9.5 GB static; +6 % speed).
+    p.sched = (pair && tiles >= 12 * (sm_count / 2)) ? 0 : 1;
     const int64_t ctas = pair ? 2 * tiles : tiles;
     p.grid = static_cast<int>(ctas < sm_count ? ctas : sm_count);
     if (pair) p.grid &= ~1;

@@ -257,6 +257,49 @@ __device__ __forceinline__ void tma_load_weight_slab_pair(void *smem_dst, const 
   }
 }
 
+// L2 eviction-priority policies for the cache-hinted loads below
+// (createpolicy.fractional with fraction 1.0: every line the load touches).
+__device__ __forceinline__ uint64_t l2_policy_evict_last() {
+  uint64_t pol;
+  asm volatile("createpolicy.fractional.L2::evict_last.b64 %0, 1.0;" : "=l"(pol));
+  return pol;
+}
+
+__device__ __forceinline__ uint64_t l2_policy_evict_first() {
+  uint64_t pol;
+  asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(pol));
+  return pol;
+}
+
+// Pair loads with an L2 cache policy.
+__device__ __forceinline__ void tma_load_2d_pair_hint(void *smem_dst, const CUtensorMap *map, uint32_t bar_cluster,
+                                                      int32_t c0, int32_t c1, uint64_t policy) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint "
+      "[%0], [%1, {%3, %4}], [%2], %5;" ::"r"(smem_u32(smem_dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(bar_cluster), "r"(c0), "r"(c1), "l"(policy)
+      : "memory");
+}
+
+__device__ __forceinline__ void tma_load_3d_pair_hint(void *smem_dst, const CUtensorMap *map, uint32_t bar_cluster,
+                                                      int32_t c0, int32_t c1, int32_t c2, uint64_t policy) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint "
+      "[%0], [%1, {%3, %4, %5}], [%2], %6;" ::"r"(smem_u32(smem_dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(bar_cluster), "r"(c0), "r"(c1), "r"(c2), "l"(policy)
+      : "memory");
+}
+
+__device__ __forceinline__ void tma_load_weight_slab_pair_hint(void *smem_dst, const CUtensorMap *map,
+                                                               uint32_t bar_cluster, int n, int k, bool slab_major,
+                                                               uint64_t policy) {
+  if (slab_major) {
+    tma_load_3d_pair_hint(smem_dst, map, bar_cluster, 0, k, n >> 6, policy);
+  } else {
+    tma_load_2d_pair_hint(smem_dst, map, bar_cluster, n, k, policy);
+  }
+}
+
 // TMEM allocation for a CTA pair: issued by the same warp in both CTAs,
 // with the same shared-memory slot offset.
 __device__ __forceinline__ void tmem_alloc_pair(uint32_t *smem_slot, uint32_t ncols) {

@@ -82,12 +82,34 @@ __device__ __forceinline__ bool item_to_work(const TcParams &p, int n_pairs, int
   return true;
 }
 
+// Row block and column tile of a tile index: bands of p.group_m row blocks,
+// row block fastest inside a band (the last band may be narrower).
+__device__ __forceinline__ void tile_coords(const TcParams &p, int tile, int &mt, int &nt) {
+  const int per_band = p.group_m * p.n_tiles;
+  const int band = tile / per_band;
+  const int r = tile - band * per_band;
+  const int rows = min(p.group_m, p.m_tiles - band * p.group_m);
+  mt = band * p.group_m + r % rows;
+  nt = r / rows;
+}
+
 // Static schedule: pair `pair` takes items pair, pair + pairs, ...
 template <int TILE_N>
 __device__ __forceinline__ bool get_work(const TcParams &p, int pair, int n_pairs, int idx, Work &w) {
   return item_to_work<TILE_N>(p, n_pairs, pair + idx * n_pairs, w);
 }
 
+#ifndef LLK_TC2_BAND_BLOCKS
+#define LLK_TC2_BAND_BLOCKS 8
+#endif
+#ifndef LLK_TC2_HINTS
+#define LLK_TC2_HINTS 0
+#endif
+// Row blocks per band of the tile order.  A wave of P pairs then covers
+// g row blocks x P/g column tiles; its L2 footprint, g X blocks plus P/g
+// weight tiles (both 256 x K bf16), is smallest at g = sqrt(P) ~ 8.6 for
+// 74 pairs, whatever K is.
+constexpr int kBandBlocks = LLK_TC2_BAND_BLOCKS;
 constexpr int kRing = 8;  // work items in flight between the leader's draw and the last role reading it
 
 struct __align__(8) PairTail {
@@ -215,6 +237,10 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (warp == 0) {
     if (lane == 0) {
       const uint32_t leader_full = map_shared_rank(smem_u32(&st->full[0]), 0);
+#if LLK_TC2_HINTS
+      const uint64_t pol_x = l2_policy_evict_last();
+      const uint64_t pol_w = l2_policy_evict_first();
+#endif
       uint32_t stage = 0, phase = 0, issued = 0;
       bool ok = true;
       Work w;
@@ -222,8 +248,10 @@ __global__ void __launch_bounds__(kThreads, 1)
       bool drew_end = false;
       for (int idx = 0; ok && next_work<kTileN>(p, st, rank, ROLE_PRODUCER, pair, n_pairs, idx, w, abort, ok, posted, drew_end);
            ++idx) {
-        const int m0 = (w.tile % p.m_tiles) * (2 * kRows) + static_cast<int>(rank) * kRows;
-        const int n0 = (w.tile / p.m_tiles) * kTileN + w.c0;
+        int mt, nt;
+        tile_coords(p, w.tile, mt, nt);
+        const int m0 = mt * (2 * kRows) + static_cast<int>(rank) * kRows;
+        const int n0 = nt * kTileN + w.c0;
         // B columns this CTA supplies: SwiGLU w.wn of its matrix (leader Wg,
         // peer Wu); matmul w.wn/2, the peer's after the leader's.
         const int cta_cols = kSwiglu ? w.wn : w.wn / 2;
@@ -240,12 +268,24 @@ __global__ void __launch_bounds__(kThreads, 1)
           const uint32_t bar = leader_full + stage * 8u;
           if (rank == 0) mbar_arrive_expect_tx(&st->full[stage], stage_tx);
           const int k0 = kb * kBK;
-          tma_load_2d_pair(sa, &tm_a, bar, k0, m0);
           const CUtensorMap *wmap = (kSwiglu && rank == 1) ? &tm_b1 : &tm_b0;
           // A 32-column part still loads a whole 64-column box (the MMA reads
           // the first 32); its start stays 64-byte aligned.
+#if LLK_TC2_HINTS
+          if (LLK_TC2_HINTS & 1) tma_load_2d_pair_hint(sa, &tm_a, bar, k0, m0, pol_x);
+          else tma_load_2d_pair(sa, &tm_a, bar, k0, m0);
+          if (LLK_TC2_HINTS & 2) {
+            tma_load_weight_slab_pair_hint(sb, wmap, bar, nb, k0, p.slab_major, pol_w);
+            if (slabs == 2) tma_load_weight_slab_pair_hint(sb + kSlabBytes, wmap, bar, nb + 64, k0, p.slab_major, pol_w);
+          } else {
+            tma_load_weight_slab_pair(sb, wmap, bar, nb, k0, p.slab_major);
+            if (slabs == 2) tma_load_weight_slab_pair(sb + kSlabBytes, wmap, bar, nb + 64, k0, p.slab_major);
+          }
+#else
+          tma_load_2d_pair(sa, &tm_a, bar, k0, m0);
           tma_load_weight_slab_pair(sb, wmap, bar, nb, k0, p.slab_major);
           if (slabs == 2) tma_load_weight_slab_pair(sb + kSlabBytes, wmap, bar, nb + 64, k0, p.slab_major);
+#endif
           ++issued;
           if (++stage == kStages) {
             stage = 0;
@@ -325,8 +365,10 @@ __global__ void __launch_bounds__(kThreads, 1)
       const uint32_t acc = local & 1;
       if (!mbar_wait_bounded(&st->tmem_full[acc], (local >> 1) & 1, abort, LLK_ERR_TIMEOUT, kWaitLimitNs)) break;
       tc_fence_after();
-      const int m0 = (w.tile % p.m_tiles) * (2 * kRows) + static_cast<int>(rank) * kRows;
-      const int n0 = (w.tile / p.m_tiles) * kTileN + w.c0;
+      int mt, nt;
+      tile_coords(p, w.tile, mt, nt);
+      const int m0 = mt * (2 * kRows) + static_cast<int>(rank) * kRows;
+      const int n0 = nt * kTileN + w.c0;
       const int row = m0 + row_in_tile;
       const uint32_t t_row = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + acc * kMmaN;
       if (kSwiglu) {
@@ -480,6 +522,7 @@ cudaError_t launch_pair_mode(const CUtensorMap &a, const CUtensorMap &b0, const 
   // whole tile), so a part costs (1 + 1/g) / 2 tile-times.  The last wave
   // then takes ceil(left * g / pairs) * (1 + 1/g) / 2; pick the g that
   // makes it shortest (ties: the wider tiles).
+  p.group_m = kBandBlocks < p.m_tiles ? kBandBlocks : p.m_tiles;
   p.dp_waves = p.num_tiles / pairs;
   const int left = p.num_tiles - p.dp_waves * pairs;
   int g = 1;

@@ -35,6 +35,10 @@ struct TcParams {
   int dynamic;
   int n_items;
   int *sched_counter;
+  // Tile order (CTA-pair kernel, filled by tc2_launch): tiles run in bands of
+  // group_m row blocks; inside a band the row block varies fastest, then the
+  // column tile, so one band's X rows stay in L2 while the band sweeps N.
+  int group_m;
 };
 
 int tc_smem_bytes();

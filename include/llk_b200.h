@@ -267,7 +267,7 @@ typedef struct llk_launch_plan {
   int grid;      /* CTAs launched */
   int threads;   /* threads per CTA */
   int smem_bytes;
-  int sched;     /* CTA-pair kernel: 1 = static round-robin (built-in), 0 = dynamic work counter */
+  int sched;     /* CTA-pair kernel: 1 = static round-robin, 0 = dynamic work counter (built-in: from 12 waves of tiles) */
 } llk_launch_plan;
 
 uint64_t llk_kernel_key_hash(const llk_kernel_key *key);

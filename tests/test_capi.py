@@ -99,6 +99,18 @@ def test_plan_cache_lru_and_stats():
         llk.cache_clear()
 
 
+def test_pair_schedule_choice_by_waves():
+    """CTA-pair plans: static round-robin below 12 waves of tiles (config 3:
+    688 tiles, 9.3 waves of 74 pairs), the dynamic work counter from there
+    on (config 5: 7168 tiles)."""
+    llk.cache_clear()
+    assert llk.KernelKey(N=11008, K=4096, M_bucket=4).plan(2048)["sched"] == 1
+    assert llk.KernelKey(N=28672, K=8192, M_bucket=4).plan(8192)["sched"] == 0
+    mm = llk.KernelKey(operation=capi.LLK_OP_MATMUL, N=4096, K=4096, M_bucket=4, output_type=capi.LLK_DTYPE_FP32)
+    assert mm.plan(4096)["sched"] == 1
+    llk.cache_clear()
+
+
 def test_shape_errors_reported_before_device_use():
     # LLKOps.cpp:42-83 rules: M/K/N mismatches are LLK_ERR_SHAPE even with no GPU
     x = np.zeros((4, 8), np.uint16)

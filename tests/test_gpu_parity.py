@@ -459,3 +459,44 @@ def test_cta_pair_and_single_cta_kernels_agree(M, K, N, op):
     finally:
         key.insert_plan(**base)
     assert rel_err(host(y_one), ref) < 1e-5
+
+
+@pytest.mark.parametrize("M,K,N,op", [(2816, 8192, 1000, "swiglu"), (2600, 16384, 640, "swiglu"),
+                                      (2600, 16384, 704, "matmul")])
+def test_pair_kernel_row_bands(M, K, N, op):
+    """Large K makes the CTA-pair kernel run its tiles in bands of row blocks
+    (8 blocks at K = 8192, 4 at K = 16384; the last band narrower): the result
+    must match FP64 points and the one-CTA kernel (no bands)."""
+    if op == "swiglu":
+        x, wg, wu = dg.swiglu_inputs(M, K, N, 1.0 / math.sqrt(K), 1.0, seed=K + 3)
+        run = lambda: llk.fused_swiglu(dev(x), dev(wg), dev(wu), out_dtype="f32", variant="tc")  # noqa: E731
+        key = llk.KernelKey(N=N, K=K, M_bucket=llk.classify_m(M), output_type=capi.LLK_DTYPE_FP32)
+    else:
+        x, wg = dg.matmul_inputs(M, K, N, seed=K + 4)
+        run = lambda: llk.matmul(dev(x), dev(wg), variant="tc")  # noqa: E731
+        key = llk.KernelKey(operation=capi.LLK_OP_MATMUL, N=N, K=K, M_bucket=llk.classify_m(M),
+                            output_type=capi.LLK_DTYPE_FP32)
+    base = key.plan(M)
+    assert base["block_m"] == 256
+    y_pair = run()
+    torch.cuda.synchronize()
+    llk.synchronize(0)
+    key.insert_plan(**dict(base, block_m=128, grid=148, stages=4))
+    try:
+        y_one = run()
+        torch.cuda.synchronize()
+        llk.synchronize(0)
+    finally:
+        key.insert_plan(**base)
+    yp, yo = host(y_pair), host(y_one)
+    assert rel_err(yp, yo) < 1e-5
+    rng = np.random.default_rng(K)
+    rows = np.concatenate([rng.integers(0, M, 3000), np.arange(M)])
+    cols = np.concatenate([rng.integers(0, N, 3000), rng.integers(0, N, M)])
+    if op == "swiglu":
+        ref = oracle.swiglu_fp64_points(x, wg, wu, rows, cols)
+    else:
+        xa = dg.bf16_bits_to_f32(x).astype(np.float64)
+        wa = dg.bf16_bits_to_f32(wg).astype(np.float64)
+        ref = np.einsum("ik,ki->i", xa[rows], wa[:, cols])
+    assert float(np.abs(yp[rows, cols] - ref).max() / np.abs(ref).max()) <= TOL_F32
