@@ -14,6 +14,9 @@ from .swiglu import (  # noqa: F401
     KernelKey,
     PackedWeights,
     cache_clear,
+    cache_level_clear,
+    cache_level_set_max_entries,
+    cache_level_stats,
     cache_set_max_entries,
     cache_stats,
     classify_m,
@@ -24,6 +27,7 @@ from .swiglu import (  # noqa: F401
     swiglu_c_abi,
     synchronize,
     tensor2d,
+    weight_key,
 )
 
 __version__ = "0.1.0"

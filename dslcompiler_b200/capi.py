@@ -24,6 +24,7 @@ LLK_ERR_ARG = 6
 LLK_ERR_DEVICE = 7
 LLK_ERR_UNSUPPORTED = 8
 LLK_ERR_NOMEM = 9
+LLK_ERR_NOT_FOUND = 10
 
 # enum llk_dtype (KernelKey.h DType)
 LLK_DTYPE_BF16 = 0
@@ -77,6 +78,17 @@ class KernelKeyC(ctypes.Structure):
                 ("schedule_version", ctypes.c_uint64)]
 
 
+class WeightKeyC(ctypes.Structure):
+    """WeightKey (include/LLK/Runtime/KernelKey.h:112-124)."""
+    _fields_ = [("weight_ptr", ctypes.c_void_p), ("shape_hash", ctypes.c_uint64), ("BK", ctypes.c_int64),
+                ("BN", ctypes.c_int64)]
+
+
+class PackedLayout(ctypes.Structure):
+    _fields_ = [("wg", ctypes.c_void_p), ("wu", ctypes.c_void_p), ("device", ctypes.c_int), ("box_n", ctypes.c_int),
+                ("box_k", ctypes.c_int), ("slab_stride_bytes", ctypes.c_int64)]
+
+
 class LaunchPlan(ctypes.Structure):
     _fields_ = [(n, ctypes.c_int) for n in ("variant", "block_m", "block_n", "block_k", "stages", "split_k", "grid",
                                             "threads", "smem_bytes", "sched")]
@@ -102,12 +114,20 @@ PROTOTYPES = {
     "llk_packed_weights_free": (None, [_vp]),
     "llk_packed_weights_info": (_i, [_vp, _P(_i64), _P(_i64), _P(_i64)]),
     "llk_swiglu_packed": (_i, [_P(Tensor2D), _vp, _P(Tensor2D), _P(KernelContext), _P(GpuContext)]),
+    "llk_packed_weights_layout": (_i, [_vp, _P(PackedLayout)]),
+    "llk_weight_key_for": (_i, [_P(Tensor2D), _P(Tensor2D), _P(WeightKeyC)]),
+    "llk_lookup_packed_weights": (_i, [_P(WeightKeyC), _P(_vp)]),
+    "llk_insert_packed_weights": (_i, [_P(WeightKeyC), _vp]),
     "llk_shard_columns": (_i, [_i64, _i, _i, _P(_i64), _P(_i64)]),
     "llk_gather_columns": (_i, [_vp, _i, _i64, _i64, _P(_i64), _vp, _i64, _i, _P(GpuContext)]),
     "llk_cuda_probe": (_i, [_i, _P(CudaTarget)]),
     "llk_kernel_key_hash": (_u64, [_P(KernelKeyC)]),
     "llk_plan_lookup": (_i, [_P(KernelKeyC), _i64, _P(LaunchPlan)]),
     "llk_plan_insert": (_i, [_P(KernelKeyC), _P(LaunchPlan)]),
+    "llk_plan_find": (_i, [_P(KernelKeyC), _P(LaunchPlan)]),
+    "llk_cache_level_stats": (_i, [_i, _P(_u64), _P(_u64), _P(_u64), _P(_u64)]),
+    "llk_cache_level_set_max_entries": (_i, [_i, _u64]),
+    "llk_cache_level_clear": (_i, [_i]),
     "llk_cache_stats": (None, [_P(_u64), _P(_u64), _P(_u64)]),
     "llk_cache_set_max_entries": (None, [_u64]),
     "llk_cache_clear": (None, []),

@@ -10,6 +10,7 @@
 #include <cuda_runtime.h>
 #include <cudaTypedefs.h>
 
+#include <atomic>
 #include <cstdint>
 #include <cstdlib>
 #include <cstring>
@@ -702,6 +703,7 @@ const char *llk_status_string(int s) {
     case LLK_ERR_DEVICE: return "no usable sm_100 device";
     case LLK_ERR_UNSUPPORTED: return "unsupported request";
     case LLK_ERR_NOMEM: return "out of memory / scratch too small";
+    case LLK_ERR_NOT_FOUND: return "no cache entry";
     default: return "unknown status";
   }
 }
@@ -786,6 +788,7 @@ struct llk_packed_weights {
   void *wg;  // device, slab-major
   void *wu;
   int64_t bytes;
+  std::atomic<int> refs{1};  // holders: the packing caller, lookups, the L4 cache
 };
 
 static int copy_weight_slabs(void *dst, int64_t K, int64_t N, const Tensor2D *w, cudaStream_t stream) {
@@ -852,6 +855,7 @@ int llk_pack_weights(const Tensor2D *wg, const Tensor2D *wu, const llk_gpu_conte
 
 void llk_packed_weights_free(llk_packed_weights *pw) {
   if (!pw) return;
+  if (pw->refs.fetch_sub(1, std::memory_order_acq_rel) > 1) return;
   int cur = 0;
   cudaGetDevice(&cur);
   cudaSetDevice(pw->device);
@@ -866,6 +870,17 @@ int llk_packed_weights_info(const llk_packed_weights *pw, int64_t *K, int64_t *N
   if (K) *K = pw->K;
   if (N) *N = pw->N;
   if (bytes) *bytes = pw->bytes;
+  return LLK_OK;
+}
+
+int llk_packed_weights_layout(const llk_packed_weights *pw, llk_packed_layout *out) {
+  if (!pw || !out) return LLK_ERR_ARG;
+  out->wg = pw->wg;
+  out->wu = pw->wu;
+  out->device = pw->device;
+  out->box_n = 64;
+  out->box_k = 64;
+  out->slab_stride_bytes = pw->K * 64 * 2;
   return LLK_OK;
 }
 
@@ -1018,6 +1033,184 @@ void llk_cache_clear(void) {
 uint64_t llk_cache_size(void) {
   std::lock_guard<std::mutex> lk(g_cache.mu);
   return g_cache.lru.size();
+}
+
+int llk_plan_find(const llk_kernel_key *key, llk_launch_plan *out) {
+  if (!key || !out) return LLK_ERR_ARG;
+  const std::string kb = key_bytes(*key);
+  std::lock_guard<std::mutex> lk(g_cache.mu);
+  auto it = g_cache.index.find(kb);
+  if (it == g_cache.index.end()) {
+    ++g_cache.misses;
+    return LLK_ERR_NOT_FOUND;
+  }
+  ++g_cache.hits;
+  g_cache.lru.splice(g_cache.lru.begin(), g_cache.lru, it->second);
+  *out = it->second->plan;
+  return LLK_OK;
+}
+
+int llk_weight_key_for(const Tensor2D *wg, const Tensor2D *wu, llk_weight_key *out) {
+  if (!wg || !wu || !out) return LLK_ERR_ARG;
+  std::memset(out, 0, sizeof(*out));
+  out->weight_ptr = wg->data;
+  // splitmix64 finaliser over the fields that tell two packings apart
+  auto mix = [](uint64_t x) {
+    x = (x ^ (x >> 30)) * 0xbf58476d1ce4e5b9ull;
+    x = (x ^ (x >> 27)) * 0x94d049bb133111ebull;
+    return x ^ (x >> 31);
+  };
+  uint64_t h = 0x6a09e667f3bcc909ull;
+  for (uint64_t v : {static_cast<uint64_t>(wg->dim0), static_cast<uint64_t>(wg->dim1),
+                     static_cast<uint64_t>(wg->stride0), static_cast<uint64_t>(wu->stride0),
+                     static_cast<uint64_t>(reinterpret_cast<uintptr_t>(wu->data))})
+    h = mix(h ^ v);
+  out->shape_hash = h;
+  out->BK = 64;
+  out->BN = 64;
+  return LLK_OK;
+}
+
+}  // extern "C"
+
+namespace {
+struct WeightCache {
+  struct Entry {
+    std::string key;
+    llk_packed_weights *pw;
+  };
+  std::list<Entry> lru;
+  std::unordered_map<std::string, std::list<Entry>::iterator> index;
+  size_t max_entries = 64;
+  uint64_t hits = 0, misses = 0, evictions = 0;
+  std::mutex mu;
+};
+WeightCache g_wcache;
+
+std::string wkey_bytes(const llk_weight_key &k) {
+  // field by field: the struct's padding is not part of the key
+  std::string b;
+  const uintptr_t p = reinterpret_cast<uintptr_t>(k.weight_ptr);
+  b.append(reinterpret_cast<const char *>(&p), sizeof(p));
+  b.append(reinterpret_cast<const char *>(&k.shape_hash), sizeof(k.shape_hash));
+  b.append(reinterpret_cast<const char *>(&k.BK), sizeof(k.BK));
+  b.append(reinterpret_cast<const char *>(&k.BN), sizeof(k.BN));
+  return b;
+}
+
+// Drops entries beyond the maximum; returns the handles to release outside
+// the lock (freeing device memory synchronises the device).
+std::vector<llk_packed_weights *> wcache_trim() {
+  std::vector<llk_packed_weights *> out;
+  while (g_wcache.lru.size() > g_wcache.max_entries) {
+    out.push_back(g_wcache.lru.back().pw);
+    g_wcache.index.erase(g_wcache.lru.back().key);
+    g_wcache.lru.pop_back();
+    ++g_wcache.evictions;
+  }
+  return out;
+}
+
+void release_all(const std::vector<llk_packed_weights *> &v) {
+  for (llk_packed_weights *pw : v) llk_packed_weights_free(pw);
+}
+}  // namespace
+
+extern "C" {
+
+int llk_lookup_packed_weights(const llk_weight_key *key, llk_packed_weights **out) {
+  if (!key || !out) return LLK_ERR_ARG;
+  *out = nullptr;
+  const std::string kb = wkey_bytes(*key);
+  std::lock_guard<std::mutex> lk(g_wcache.mu);
+  auto it = g_wcache.index.find(kb);
+  if (it == g_wcache.index.end()) {
+    ++g_wcache.misses;
+    return LLK_ERR_NOT_FOUND;
+  }
+  ++g_wcache.hits;
+  g_wcache.lru.splice(g_wcache.lru.begin(), g_wcache.lru, it->second);
+  it->second->pw->refs.fetch_add(1, std::memory_order_relaxed);
+  *out = it->second->pw;
+  return LLK_OK;
+}
+
+int llk_insert_packed_weights(const llk_weight_key *key, llk_packed_weights *pw) {
+  if (!key || !pw) return LLK_ERR_ARG;
+  const std::string kb = wkey_bytes(*key);
+  std::vector<llk_packed_weights *> drop;
+  {
+    std::lock_guard<std::mutex> lk(g_wcache.mu);
+    pw->refs.fetch_add(1, std::memory_order_relaxed);
+    auto it = g_wcache.index.find(kb);
+    if (it != g_wcache.index.end()) {
+      drop.push_back(it->second->pw);
+      it->second->pw = pw;
+      g_wcache.lru.splice(g_wcache.lru.begin(), g_wcache.lru, it->second);
+    } else {
+      g_wcache.lru.push_front({kb, pw});
+      g_wcache.index[kb] = g_wcache.lru.begin();
+      drop = wcache_trim();
+    }
+  }
+  release_all(drop);
+  return LLK_OK;
+}
+
+int llk_cache_level_stats(int level, uint64_t *hits, uint64_t *misses, uint64_t *evictions, uint64_t *size) {
+  uint64_t h = 0, m = 0, e = 0, n = 0;
+  if (level == 3) {
+    std::lock_guard<std::mutex> lk(g_cache.mu);
+    h = g_cache.hits, m = g_cache.misses, e = g_cache.evictions, n = g_cache.lru.size();
+  } else if (level == 4) {
+    std::lock_guard<std::mutex> lk(g_wcache.mu);
+    h = g_wcache.hits, m = g_wcache.misses, e = g_wcache.evictions, n = g_wcache.lru.size();
+  } else if (level != 1 && level != 2) {
+    return LLK_ERR_ARG;
+  }
+  if (hits) *hits = h;
+  if (misses) *misses = m;
+  if (evictions) *evictions = e;
+  if (size) *size = n;
+  return LLK_OK;
+}
+
+int llk_cache_level_set_max_entries(int level, uint64_t max_entries) {
+  if (level == 3) {
+    llk_cache_set_max_entries(max_entries);
+    return LLK_OK;
+  }
+  if (level == 4) {
+    std::vector<llk_packed_weights *> drop;
+    {
+      std::lock_guard<std::mutex> lk(g_wcache.mu);
+      g_wcache.max_entries = max_entries;
+      drop = wcache_trim();
+    }
+    release_all(drop);
+    return LLK_OK;
+  }
+  return level == 1 || level == 2 ? LLK_ERR_UNSUPPORTED : LLK_ERR_ARG;
+}
+
+int llk_cache_level_clear(int level) {
+  if (level == 3) {
+    llk_cache_clear();
+    return LLK_OK;
+  }
+  if (level == 4) {
+    std::vector<llk_packed_weights *> drop;
+    {
+      std::lock_guard<std::mutex> lk(g_wcache.mu);
+      for (auto &e : g_wcache.lru) drop.push_back(e.pw);
+      g_wcache.lru.clear();
+      g_wcache.index.clear();
+      g_wcache.hits = g_wcache.misses = g_wcache.evictions = 0;
+    }
+    release_all(drop);
+    return LLK_OK;
+  }
+  return level == 1 || level == 2 ? LLK_OK : LLK_ERR_ARG;
 }
 
 }  // extern "C"

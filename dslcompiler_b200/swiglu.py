@@ -155,6 +155,37 @@ class PackedWeights:
         check(lib().llk_packed_weights_info(self._h, ctypes.byref(K), ctypes.byref(N), ctypes.byref(B)))
         self.K, self.N, self.nbytes = K.value, N.value, B.value
 
+    @classmethod
+    def cached(cls, wg, wu, *, device=None, stream=None) -> "PackedWeights":
+        """The packed pair for (wg, wu) from the library's L4 cache, keyed by
+        WeightKey (the weights' pointers, shapes and strides); packed and
+        inserted on a miss.  The cache keeps its own reference, so the
+        device copy outlives this object until evicted (see
+        :func:`cache_level_set_max_entries`).  A caller that changes the
+        weights in place must :meth:`repack` -- the key does not see the
+        contents."""
+        key = weight_key(wg, wu)
+        h = ctypes.c_void_p()
+        st = lib().llk_lookup_packed_weights(ctypes.byref(key), ctypes.byref(h))
+        if st == capi.LLK_OK:
+            self = cls.__new__(cls)
+            self._h = h
+            K, N, B = ctypes.c_int64(), ctypes.c_int64(), ctypes.c_int64()
+            check(lib().llk_packed_weights_info(self._h, ctypes.byref(K), ctypes.byref(N), ctypes.byref(B)))
+            self.K, self.N, self.nbytes = K.value, N.value, B.value
+            return self
+        if st != capi.LLK_ERR_NOT_FOUND:
+            check(st, "llk_lookup_packed_weights")
+        self = cls(wg, wu, device=device, stream=stream)
+        check(lib().llk_insert_packed_weights(ctypes.byref(key), self._h), "llk_insert_packed_weights")
+        return self
+
+    def layout(self) -> dict:
+        """Device pointers and box geometry of the packed pair."""
+        L = capi.PackedLayout()
+        check(lib().llk_packed_weights_layout(self._h, ctypes.byref(L)), "llk_packed_weights_layout")
+        return {f: getattr(L, f) for f, _ in capi.PackedLayout._fields_}
+
     def repack(self, wg, wu, stream=None):
         tg, tu = tensor2d(wg), tensor2d(wu)
         g = gpu_context(-1, _stream_of(wg, stream))
@@ -181,6 +212,31 @@ class PackedWeights:
             self.close()
         except Exception:
             pass
+
+
+def weight_key(wg, wu) -> capi.WeightKeyC:
+    """WeightKey of a (Wg, Wu) pair (llk_weight_key_for)."""
+    k = capi.WeightKeyC()
+    tg, tu = tensor2d(wg), tensor2d(wu)
+    check(lib().llk_weight_key_for(ctypes.byref(tg), ctypes.byref(tu), ctypes.byref(k)), "llk_weight_key_for")
+    return k
+
+
+def cache_level_stats(level: int) -> dict:
+    """hits / misses / evictions / size of cache level 1-4 (JitCache.h
+    numbering: 3 = launch plans, 4 = packed weights)."""
+    h, m, e, n = (ctypes.c_uint64() for _ in range(4))
+    check(lib().llk_cache_level_stats(level, ctypes.byref(h), ctypes.byref(m), ctypes.byref(e), ctypes.byref(n)),
+          "llk_cache_level_stats")
+    return {"hits": h.value, "misses": m.value, "evictions": e.value, "size": n.value}
+
+
+def cache_level_set_max_entries(level: int, n: int) -> None:
+    check(lib().llk_cache_level_set_max_entries(level, n), "llk_cache_level_set_max_entries")
+
+
+def cache_level_clear(level: int) -> None:
+    check(lib().llk_cache_level_clear(level), "llk_cache_level_clear")
 
 
 def probe(device: int = -1) -> dict:
@@ -235,6 +291,16 @@ class KernelKey:
         for f, _ in capi.LaunchPlan._fields_:
             setattr(p, f, int(plan.get(f, 0)))
         check(lib().llk_plan_insert(ctypes.byref(k), ctypes.byref(p)), "llk_plan_insert")
+
+    def find(self) -> dict | None:
+        """The cached plan, or None (lookupObjectCode: builds nothing)."""
+        k = self.to_c()
+        p = capi.LaunchPlan()
+        st = lib().llk_plan_find(ctypes.byref(k), ctypes.byref(p))
+        if st == capi.LLK_ERR_NOT_FOUND:
+            return None
+        check(st, "llk_plan_find")
+        return {f: getattr(p, f) for f, _ in capi.LaunchPlan._fields_}
 
     def plan(self, M: int) -> dict:
         k = self.to_c()

@@ -73,7 +73,8 @@ enum llk_status_code {
   LLK_ERR_ARG = 6,         /* NULL pointer or bad enum value */
   LLK_ERR_DEVICE = 7,      /* no sm_100 device, or library not usable */
   LLK_ERR_UNSUPPORTED = 8, /* valid request this backend does not do */
-  LLK_ERR_NOMEM = 9        /* scratch too small / allocation failed */
+  LLK_ERR_NOMEM = 9,       /* scratch too small / allocation failed */
+  LLK_ERR_NOT_FOUND = 10   /* cache lookup without an entry */
 };
 
 /* include/LLK/Runtime/KernelKey.h:23 (DType) */
@@ -198,6 +199,47 @@ int llk_packed_weights_info(const llk_packed_weights *pw, int64_t *K, int64_t *N
 int llk_swiglu_packed(const Tensor2D *x, const llk_packed_weights *pw, Tensor2D *y, KernelContext *ctx,
                       const llk_gpu_context *gpu);
 
+/* Device layout of a packed pair: for each of Wg and Wu, ceil(N/box_n)
+ * slabs of [K][box_n] bf16 (slab s holds columns s*box_n ..), each slab
+ * contiguous, so one TMA box of box_n x box_k elements is one contiguous
+ * 8 KB block.  Pointers are device pointers on *device. */
+typedef struct llk_packed_layout {
+  void *wg;
+  void *wu;
+  int device;
+  int box_n; /* 64 columns per slab (BN) */
+  int box_k; /* 64 rows of K per TMA box / pipeline stage (BK) */
+  int64_t slab_stride_bytes; /* K * box_n * 2 */
+} llk_packed_layout;
+
+int llk_packed_weights_layout(const llk_packed_weights *pw, llk_packed_layout *out);
+
+/* ---- L4 packed-weight cache (JitCache.h:138-146; WeightKey,
+ *      KernelKey.h:112-124) ---------------------------------------------
+ * Device-resident packed pairs keyed by WeightKey, LRU-evicted beyond the
+ * level-4 maximum.  Handles are reference counted: llk_pack_weights and
+ * every hit of llk_lookup_packed_weights hand the caller one reference,
+ * released with llk_packed_weights_free; the cache holds its own reference
+ * from llk_insert_packed_weights until the entry is evicted, replaced or
+ * cleared, so a handle a caller looked up stays valid until the caller
+ * frees it.  (The reference's L4 stores a serialised host blob; this one
+ * stores the device copy the kernels read.) */
+typedef struct llk_weight_key {
+  const void *weight_ptr; /* the caller's Wg data pointer */
+  uint64_t shape_hash;    /* see llk_weight_key_for */
+  int64_t BK;             /* box rows of K (64) */
+  int64_t BN;             /* slab width (64) */
+} llk_weight_key;
+
+/* Key for the pair (wg, wu): weight_ptr = wg->data; shape_hash mixes K, N,
+ * both row strides and wu->data (two pairs sharing Wg but not Wu differ);
+ * BK = BN = 64. */
+int llk_weight_key_for(const Tensor2D *wg, const Tensor2D *wu, llk_weight_key *out);
+/* LLK_OK and a new reference in *out on a hit; LLK_ERR_NOT_FOUND on a miss. */
+int llk_lookup_packed_weights(const llk_weight_key *key, llk_packed_weights **out);
+/* The cache takes its own reference (the caller keeps theirs). */
+int llk_insert_packed_weights(const llk_weight_key *key, llk_packed_weights *pw);
+
 /* ---- column sharding (multi-GPU) --------------------------------------- */
 
 /* Columns [begin, end) of an N-column output owned by shard `index` of
@@ -278,11 +320,24 @@ int llk_plan_lookup(const llk_kernel_key *key, int64_t M, llk_launch_plan *out);
  * used).  key->thread_count carries the variant and must equal
  * plan->variant. */
 int llk_plan_insert(const llk_kernel_key *key, const llk_launch_plan *plan);
+/* Pure lookup (lookupObjectCode, JitCache.h:113): LLK_OK with the cached
+ * plan, or LLK_ERR_NOT_FOUND; builds nothing.  llk_plan_lookup is the
+ * lookupOrCompile counterpart: it builds and caches the built-in plan on a
+ * miss. */
+int llk_plan_find(const llk_kernel_key *key, llk_launch_plan *out);
 /* hits, misses, evictions of the plan cache. */
 void llk_cache_stats(uint64_t *hits, uint64_t *misses, uint64_t *evictions);
 void llk_cache_set_max_entries(uint64_t max_entries);
 void llk_cache_clear(void);
 uint64_t llk_cache_size(void);
+
+/* Per cache level, numbered as JitCache's (1 IR, 2 optimised MLIR, 3 object
+ * code, 4 packed weights): 3 is the plan cache, 4 the packed-weight cache;
+ * levels 1 and 2 have no counterpart (the kernels are compiled ahead of
+ * time) and report zeros / refuse with LLK_ERR_UNSUPPORTED. */
+int llk_cache_level_stats(int level, uint64_t *hits, uint64_t *misses, uint64_t *evictions, uint64_t *size);
+int llk_cache_level_set_max_entries(int level, uint64_t max_entries);
+int llk_cache_level_clear(int level);
 
 /* M bucket: {1}, [2,4], [5,16], [17,64], >=65 -> 0..4
  * (lib/Transforms/Common/ScheduleLoader.cpp:19-29). */

@@ -185,3 +185,57 @@ def test_c_program_runs_swiglu_on_gpu(tmp_path):
     exe = _build_c_smoke(tmp_path)
     r = subprocess.run([str(exe)], capture_output=True, text=True, timeout=120)
     assert r.returncode == 0 and r.stdout.startswith("ok 0 "), r.stdout + r.stderr
+
+
+def _build_cpp_cache_smoke(tmp_path):
+    import subprocess
+    exe = tmp_path / "jitcache_smoke"
+    cmd = ["g++", "-std=c++17", "-Wall", "-Werror", "-I", os.path.join(ROOT, "include"),
+           os.path.join(ROOT, "tests", "jitcache_smoke.cpp"), "-L", os.path.dirname(capi.LIB_PATH), "-lllk_b200",
+           "-Wl,-rpath," + os.path.dirname(capi.LIB_PATH), "-o", str(exe)]
+    subprocess.run(cmd, check=True)
+    return exe
+
+
+def test_jitcache_header_plan_levels(tmp_path):
+    """llk_b200_jitcache.hpp: JitCache's method names over the C ABI (L3
+    plans, L1/L2 always missing, L4 miss) from a C++ program."""
+    import subprocess
+    r = subprocess.run([str(_build_cpp_cache_smoke(tmp_path))], capture_output=True, text=True, timeout=120)
+    assert r.returncode == 0 and r.stdout.strip() == "ok", r.stdout + r.stderr
+
+
+@pytest.mark.gpu
+def test_jitcache_header_packed_weights_on_gpu(tmp_path):
+    import subprocess
+    r = subprocess.run([str(_build_cpp_cache_smoke(tmp_path)), "gpu"], capture_output=True, text=True, timeout=120)
+    assert r.returncode == 0 and r.stdout.strip() == "ok", r.stdout + r.stderr
+
+
+def test_weight_key_and_l4_miss():
+    """WeightKey of a pair: pointer of Wg, a hash that changes with shape,
+    strides and Wu, BK = BN = 64; an empty L4 misses."""
+    wg = np.zeros((8, 128), np.uint16)
+    wu = np.zeros((8, 128), np.uint16)
+    k1 = llk.weight_key(wg, wu)
+    assert k1.weight_ptr == wg.ctypes.data and k1.BK == 64 and k1.BN == 64
+    assert llk.weight_key(wg, wu).shape_hash == k1.shape_hash
+    assert llk.weight_key(wg, np.zeros((8, 128), np.uint16)).shape_hash != k1.shape_hash
+    assert llk.weight_key(wg[:, :64], wu[:, :64]).shape_hash != k1.shape_hash
+    llk.cache_level_clear(4)
+    h = ctypes.c_void_p()
+    assert capi.lib().llk_lookup_packed_weights(ctypes.byref(k1), ctypes.byref(h)) == capi.LLK_ERR_NOT_FOUND
+    s = llk.cache_level_stats(4)
+    assert s["misses"] == 1 and s["size"] == 0
+    assert llk.cache_level_stats(1) == {"hits": 0, "misses": 0, "evictions": 0, "size": 0}
+    with pytest.raises(capi.LLKError):
+        llk.cache_level_stats(5)
+
+
+def test_plan_find_is_pure_lookup():
+    llk.cache_clear()
+    key = llk.KernelKey(N=640, K=256, M_bucket=4)
+    assert key.find() is None
+    p = key.plan(300)
+    assert key.find() == p
+    llk.cache_clear()

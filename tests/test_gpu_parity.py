@@ -500,3 +500,32 @@ def test_pair_kernel_row_bands(M, K, N, op):
         wa = dg.bf16_bits_to_f32(wg).astype(np.float64)
         ref = np.einsum("ik,ki->i", xa[rows], wa[:, cols])
     assert float(np.abs(yp[rows, cols] - ref).max() / np.abs(ref).max()) <= TOL_F32
+
+
+def test_packed_weights_l4_cache():
+    """PackedWeights.cached: a miss packs and inserts, a hit returns the same
+    device copy (no second pack), results equal the unpacked path, and the
+    copy outlives the first handle until the cache evicts it."""
+    M, K, N = 300, 512, 640
+    x, wg, wu = dg.swiglu_inputs(M, K, N, 1.0 / math.sqrt(K), 1.0, seed=9)
+    xd, gd, ud = dev(x), dev(wg), dev(wu)
+    llk.cache_level_clear(4)
+    a = llk.PackedWeights.cached(gd, ud)
+    b = llk.PackedWeights.cached(gd, ud)
+    s = llk.cache_level_stats(4)
+    assert s["misses"] == 1 and s["hits"] == 1 and s["size"] == 1
+    assert a.layout()["wg"] == b.layout()["wg"] and a.layout()["box_n"] == 64
+    ref = llk.fused_swiglu(xd, gd, ud, out_dtype="f32")
+    a.close()  # the cache's reference keeps the device copy
+    y = b(xd, out_dtype="f32")
+    torch.cuda.synchronize()
+    llk.synchronize(0)
+    assert torch.equal(y, ref)
+    llk.cache_level_set_max_entries(4, 0)
+    assert llk.cache_level_stats(4)["size"] == 0
+    y2 = b(xd, out_dtype="f32")  # b still holds its reference
+    torch.cuda.synchronize()
+    assert torch.equal(y2, ref)
+    b.close()
+    llk.cache_level_set_max_entries(4, 64)
+    llk.cache_level_clear(4)
