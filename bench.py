@@ -368,6 +368,8 @@ def our_arm(args):
     n_sets = len(sets)
     if world > 1:
         extras["gather_y"] = gather_timing(args, dev, stream, yd, N, world, barrier, max_over_ranks)
+        extras["fused_allgather"] = fused_allgather_timing(args, dev, stream, xd, gd, ud, N, barrier, max_over_ranks,
+                                                           job_ms, extras["gather_y"]["ms"])
     cpu = None
     if not args.quick:
         del sets, xd, gd, ud, yd
@@ -443,6 +445,33 @@ def gather_timing(args, dev, stream, yd, N, world, barrier, max_over_ranks):
     recv = (world - 1) * M * width * yd.element_size()
     return {"ms": ms, "bytes_received_per_gpu": recv, "GB/s_per_gpu": recv / (ms * 1e-3) / 1e9,
             "what": "all_gather_into_tensor (NCCL) of padded Y shards + llk_gather_columns relayout"}
+
+
+def fused_allgather_timing(args, dev, stream, xd, gd, ud, N, barrier, max_over_ranks, kernel_ms, gather_ms):
+    """The full-Y path with the all-gather fused into the kernel
+    (llk_swiglu_column_parallel: each rank's epilogue stores its columns
+    into every rank's Y over NVLink, plus the entry / exit barriers), against
+    kernel + NCCL all-gather + relayout."""
+    import torch
+
+    from dslcompiler_b200.sharding import PeerGroupSwiGLU
+
+    M, K = xd.shape
+    layer = PeerGroupSwiGLU(gd, ud, N, max_rows=M, already_sharded=True, pack=False, device=dev.index)
+    for _ in range(3):
+        layer(xd)
+    torch.cuda.synchronize()
+    barrier()
+    steps = max(5, min(args.steps, 200))
+    ms = max_over_ranks(time_back_to_back(lambda i: layer(xd), steps, stream)) / steps
+    torch.cuda.synchronize()
+    barrier()
+    layer.close()
+    flops = 4.0 * M * N * K
+    return {"ms": ms, "tflops_whole_job": flops / (ms * 1e-3) / 1e12,
+            "kernel_plus_nccl_gather_ms": kernel_ms + gather_ms,
+            "tflops_kernel_plus_nccl_gather": flops / ((kernel_ms + gather_ms) * 1e-3) / 1e12,
+            "what": "llk_swiglu_column_parallel: full Y on every GPU, shards stored to peers by the kernel epilogue"}
 
 
 def single_gpu_extras(args, dev, stream, peak_tf, peak_gbs):

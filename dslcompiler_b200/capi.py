@@ -25,6 +25,7 @@ LLK_ERR_DEVICE = 7
 LLK_ERR_UNSUPPORTED = 8
 LLK_ERR_NOMEM = 9
 LLK_ERR_NOT_FOUND = 10
+LLK_IPC_HANDLE_BYTES = 64
 
 # enum llk_dtype (KernelKey.h DType)
 LLK_DTYPE_BF16 = 0
@@ -121,6 +122,11 @@ PROTOTYPES = {
     "llk_shard_columns": (_i, [_i64, _i, _i, _P(_i64), _P(_i64)]),
     "llk_gather_columns": (_i, [_vp, _i, _i64, _i64, _P(_i64), _vp, _i64, _i, _P(GpuContext)]),
     "llk_cuda_probe": (_i, [_i, _P(CudaTarget)]),
+    "llk_peer_group_create": (_i, [_i, _i, _i64, _P(GpuContext), _P(_vp), ctypes.c_char_p]),
+    "llk_peer_group_connect": (_i, [_vp, ctypes.c_char_p]),
+    "llk_peer_group_y": (_i, [_vp, _P(_vp), _P(_i64)]),
+    "llk_peer_group_destroy": (None, [_vp]),
+    "llk_swiglu_column_parallel": (_i, [_P(Tensor2D), _P(Tensor2D), _P(Tensor2D), _vp, _i64, _vp, _P(GpuContext)]),
     "llk_kernel_key_hash": (_u64, [_P(KernelKeyC)]),
     "llk_plan_lookup": (_i, [_P(KernelKeyC), _i64, _P(LaunchPlan)]),
     "llk_plan_insert": (_i, [_P(KernelKeyC), _P(LaunchPlan)]),

@@ -150,6 +150,22 @@ int encode_tmap(CUtensorMap *m, const void *base, uint64_t inner, uint64_t outer
   return r == CUDA_SUCCESS ? LLK_OK : LLK_ERR_ALIGN;
 }
 
+// Store map of an output Y [M, N] (row pitch N elements) for the staged TMA
+// stores of the CTA-pair epilogue: box {32, 32}; bf16 rows of a box are 64
+// bytes (64-byte swizzle), f32 rows 128 bytes (128-byte swizzle).
+int encode_ystore_map(CUtensorMap *m, void *base, uint64_t N, uint64_t M, int y_f32) {
+  const uint64_t el = y_f32 ? 4 : 2;
+  cuuint64_t dims[2] = {N, M};
+  cuuint64_t strides[1] = {N * el};
+  cuuint32_t box[2] = {32, 32};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = g_encode(m, y_f32 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, base, dims,
+                        strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                        y_f32 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B,
+                        CU_TENSOR_MAP_L2_PROMOTION_NONE, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS ? LLK_OK : LLK_ERR_ALIGN;
+}
+
 // Slab-major packed weights ([N/64][K][64] bf16, see llk_pack_weights) as a
 // 3-D tensor map {64, K, N/64} with a {64, 64, 1} box: every box is one
 // contiguous 8 KB block.
@@ -304,9 +320,19 @@ int encode_weight_tmap(CUtensorMap *m, const DevTensor &w) {
 
 // Y = SwiGLU(X, Wg, Wu) or C (+)= A B on device tensors.  op: LLK_OP_*.
 // Called with ds.mu held (it guards the staging buffers and the workspace).
+// Other GPUs' Y buffers (mapped here) that receive the same output columns.
+struct PeerTargets {
+  int n = 0;
+  void *y[kMaxYPeers] = {};
+  const YStoreMaps *maps = nullptr;  // TMA store maps (own Y first), when the rows allow them
+};
+
+// peers: when set, the CTA-pair kernel also stores every Y chunk to each
+// peer (fused all-gather) and *peers_done is set; other variants leave the
+// copies to the caller.
 int launch_device(DeviceState &ds, int op, const DevTensor &x, const DevTensor &wg, const DevTensor &wu,
                   const DevTensor &y, int y_f32, int accumulate, int requested, void *scratch, size_t scratch_bytes,
-                  cudaStream_t stream) {
+                  cudaStream_t stream, const PeerTargets *peers = nullptr, bool *peers_done = nullptr) {
   const int64_t M = x.rows, K = x.cols, N = wg.cols;
   if (M == 0 || N == 0) return LLK_OK;
   if (M > INT32_MAX || N > INT32_MAX || K > INT32_MAX) return LLK_ERR_SHAPE;
@@ -411,7 +437,12 @@ int launch_device(DeviceState &ds, int op, const DevTensor &x, const DevTensor &
         counter = static_cast<int *>(ds.workspace.ptr);
       }
     }
-    e = tc2_launch(mode, ta, tb0, tb1, p, max_pairs, tail_split, counter, stream);
+    if (peers) {
+      p.n_peers = peers->n;
+      for (int i = 0; i < peers->n; ++i) p.y_peers[i] = peers->y[i];
+      if (peers_done) *peers_done = true;
+    }
+    e = tc2_launch(mode, ta, tb0, tb1, p, max_pairs, tail_split, counter, stream, peers ? peers->maps : nullptr);
     return e == cudaSuccess ? LLK_OK : LLK_ERR_CUDA;
   }
   int grid = p.num_tiles < ds.sm_count ? p.num_tiles : ds.sm_count;
@@ -672,6 +703,84 @@ int run_op(int op, const Tensor2D *x, const Tensor2D *wg, const Tensor2D *wu, Te
     if (any_host) return read_and_clear_status(*ds, stream);
   }
   return LLK_OK;
+}
+
+// ------------------------------------------------- column-parallel groups
+// One per GPU of a column-parallel SwiGLU: a device allocation holding a
+// flag block and two Y buffers [M, N], exported by CUDA IPC; every rank maps
+// every other rank's allocation.  Call t computes this rank's columns, the
+// CTA-pair epilogue storing each chunk into every rank's Y buffer t % 2
+// (fused all-gather), then runs a barrier so that, in stream order, this
+// GPU's buffer holds all columns.  Alternating buffers make an entry barrier
+// unnecessary: a rank starts call t + 1 only after call t's barrier saw
+// every peer's stream reach call t, i.e. past every peer's stream-ordered
+// use of buffer (t + 1) % 2 = (t - 1) % 2.
+constexpr int kGroupMax = 8;
+constexpr size_t kFlagBytes = 4096;  // flag block at the start of each allocation
+constexpr uint64_t kBarrierLimitNs = 2000000000ull;
+
+struct BarrierArgs {
+  unsigned int *peer_slot[kGroupMax];  // rank r's flag word for this rank (in r's allocation)
+  unsigned int *own[kGroupMax];        // this rank's flag word for rank r (own allocation)
+};
+
+// Thread r < n: publish `epoch` in rank r's slot for this rank (system-scope
+// release), then wait until rank r published it here.  Bounded: after the
+// limit the status word gets LLK_ERR_TIMEOUT and the kernel returns.
+__global__ void peer_barrier_kernel(BarrierArgs a, int n, unsigned int epoch, int *status) {
+  const int r = threadIdx.x;
+  if (r >= n) return;
+  __threadfence_system();
+  asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(a.peer_slot[r]), "r"(epoch) : "memory");
+  uint64_t t0;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t0));
+  while (true) {
+    unsigned int v;
+    asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(a.own[r]) : "memory");
+    if (static_cast<int>(v - epoch) >= 0) break;
+    uint64_t t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    if (t - t0 > kBarrierLimitNs) {
+      atomicExch(status, LLK_ERR_TIMEOUT);
+      break;
+    }
+    __nanosleep(200);
+  }
+}
+
+}  // namespace
+
+struct llk_peer_group {
+  int device = -1, n = 0, rank = 0;
+  char *local = nullptr;          // [flags 4 KB][Y buffer 0][Y buffer 1]
+  size_t y_bytes = 0;             // capacity of one Y buffer (multiple of 256)
+  char *base[kGroupMax] = {};     // every rank's allocation as mapped here
+  bool connected = false;
+  unsigned int epoch = 0;
+  cudaIpcMemHandle_t handle;
+};
+
+namespace {
+
+// Flag words of barrier `which` at [8 * which, 8 * which + 8), one per rank.
+BarrierArgs barrier_args(const llk_peer_group &g, int which) {
+  BarrierArgs a;
+  std::memset(&a, 0, sizeof(a));
+  for (int r = 0; r < g.n; ++r) {
+    a.peer_slot[r] = reinterpret_cast<unsigned int *>(g.base[r]) + which * kGroupMax + g.rank;
+    a.own[r] = reinterpret_cast<unsigned int *>(g.local) + which * kGroupMax + r;
+  }
+  return a;
+}
+
+DevTensor dev_tensor(const Tensor2D &t) {
+  DevTensor d;
+  d.data = t.data;
+  d.rows = t.dim0;
+  d.cols = t.dim1;
+  d.ld = t.stride0;
+  d.inner = t.stride1;
+  return d;
 }
 
 }  // namespace
@@ -1211,6 +1320,164 @@ int llk_cache_level_clear(int level) {
     return LLK_OK;
   }
   return level == 1 || level == 2 ? LLK_OK : LLK_ERR_ARG;
+}
+
+
+// ------------------------------------------------- column-parallel groups
+int llk_peer_group_create(int n_ranks, int rank, int64_t y_bytes, const llk_gpu_context *gpu, llk_peer_group **out,
+                          unsigned char *ipc_handle) {
+  if (!out || !ipc_handle || n_ranks < 1 || n_ranks > kGroupMax || rank < 0 || rank >= n_ranks || y_bytes < 0)
+    return LLK_ERR_ARG;
+  *out = nullptr;
+  int dev, rc;
+  if ((rc = resolve_device(gpu, &dev)) != LLK_OK) return rc;
+  DeviceState *ds;
+  if ((rc = device_init(dev, &ds)) != LLK_OK) return rc;
+  llk_peer_group *g = new llk_peer_group();
+  g->device = dev;
+  g->n = n_ranks;
+  g->rank = rank;
+  g->y_bytes = (static_cast<size_t>(y_bytes) + 255) & ~static_cast<size_t>(255);
+  if (cudaMalloc(&g->local, kFlagBytes + 2 * g->y_bytes) != cudaSuccess) {
+    delete g;
+    return LLK_ERR_NOMEM;
+  }
+  if (cudaMemset(g->local, 0, kFlagBytes) != cudaSuccess || cudaIpcGetMemHandle(&g->handle, g->local) != cudaSuccess) {
+    cudaFree(g->local);
+    delete g;
+    return LLK_ERR_CUDA;
+  }
+  std::memcpy(ipc_handle, &g->handle, sizeof(g->handle));
+  g->base[rank] = g->local;
+  *out = g;
+  return LLK_OK;
+}
+
+int llk_peer_group_connect(llk_peer_group *g, const unsigned char *all_handles) {
+  if (!g || !all_handles) return LLK_ERR_ARG;
+  if (g->connected) return LLK_OK;
+  if (cudaSetDevice(g->device) != cudaSuccess) return LLK_ERR_DEVICE;
+  for (int r = 0; r < g->n; ++r) {
+    if (r == g->rank) continue;
+    cudaIpcMemHandle_t h;
+    std::memcpy(&h, all_handles + static_cast<size_t>(r) * LLK_IPC_HANDLE_BYTES, sizeof(h));
+    void *p = nullptr;
+    if (cudaIpcOpenMemHandle(&p, h, cudaIpcMemLazyEnablePeerAccess) != cudaSuccess) {
+      cudaGetLastError();
+      for (int q = 0; q < r; ++q)
+        if (q != g->rank && g->base[q]) cudaIpcCloseMemHandle(g->base[q]);
+      for (int q = 0; q < g->n; ++q)
+        if (q != g->rank) g->base[q] = nullptr;
+      return LLK_ERR_CUDA;
+    }
+    g->base[r] = static_cast<char *>(p);
+  }
+  g->connected = true;
+  return LLK_OK;
+}
+
+int llk_peer_group_y(const llk_peer_group *g, void **y, int64_t *bytes) {
+  if (!g) return LLK_ERR_ARG;
+  if (y) *y = g->local + kFlagBytes + (g->epoch & 1u) * g->y_bytes;
+  if (bytes) *bytes = static_cast<int64_t>(g->y_bytes);
+  return LLK_OK;
+}
+
+void llk_peer_group_destroy(llk_peer_group *g) {
+  if (!g) return;
+  int cur = 0;
+  cudaGetDevice(&cur);
+  cudaSetDevice(g->device);
+  for (int r = 0; r < g->n; ++r)
+    if (r != g->rank && g->base[r]) cudaIpcCloseMemHandle(g->base[r]);
+  cudaFree(g->local);
+  cudaSetDevice(cur);
+  delete g;
+}
+
+int llk_swiglu_column_parallel(const Tensor2D *x, const Tensor2D *wg_shard, const Tensor2D *wu_shard,
+                               const llk_packed_weights *pw_shard, int64_t N, llk_peer_group *g,
+                               const llk_gpu_context *gpu) {
+  if (!x || !g || (!pw_shard && (!wg_shard || !wu_shard)) || N < 0) return LLK_ERR_ARG;
+  if (!g->connected) return LLK_ERR_ARG;
+  if (gpu && gpu->device >= 0 && gpu->device != g->device) return LLK_ERR_ARG;
+  const int y_f32 = (gpu && gpu->y_dtype == LLK_DTYPE_FP32) ? 1 : 0;
+  if (gpu && gpu->y_dtype != LLK_DTYPE_BF16 && gpu->y_dtype != LLK_DTYPE_FP32) return LLK_ERR_ARG;
+  const int requested = gpu ? gpu->variant : LLK_VARIANT_AUTO;
+  const int64_t M = x->dim0, K = x->dim1;
+  int64_t b, e;
+  if (llk_shard_columns(N, g->n, g->rank, &b, &e) != LLK_OK) return LLK_ERR_ARG;
+  const int64_t w = e - b;
+  const int yel = y_f32 ? 4 : 2;
+  if (static_cast<size_t>(M) * static_cast<size_t>(N) * yel > g->y_bytes) return LLK_ERR_NOMEM;
+  // shapes: X [M, K]; this rank's weights [K, e - b]
+  DevTensor dg, du;
+  if (pw_shard) {
+    if (pw_shard->K != K || pw_shard->N != w || pw_shard->device != g->device) return LLK_ERR_SHAPE;
+    dg.data = pw_shard->wg;
+    du.data = pw_shard->wu;
+    dg.rows = du.rows = K;
+    dg.cols = du.cols = w;
+    dg.ld = du.ld = 64;
+    dg.inner = du.inner = 1;
+    dg.slab_major = du.slab_major = 1;
+  } else {
+    if (wg_shard->dim0 != K || wg_shard->dim1 != w || wu_shard->dim0 != K || wu_shard->dim1 != w)
+      return LLK_ERR_SHAPE;
+    if (!is_device_ptr(wg_shard->data) || !is_device_ptr(wu_shard->data)) return LLK_ERR_ARG;
+    dg = dev_tensor(*wg_shard);
+    du = dev_tensor(*wu_shard);
+  }
+  if (M > 0 && !is_device_ptr(x->data)) return LLK_ERR_ARG;
+  DeviceState *ds;
+  int rc;
+  if ((rc = device_init(g->device, &ds)) != LLK_OK) return rc;
+  cudaStream_t stream = gpu ? static_cast<cudaStream_t>(gpu->stream) : nullptr;
+  ++g->epoch;
+  const size_t ybuf = kFlagBytes + (g->epoch & 1u) * g->y_bytes;
+  char *y_local = g->local + ybuf;
+  BarrierArgs exit_ = barrier_args(*g, 0);
+  if (M > 0 && w > 0) {
+    DevTensor dx = dev_tensor(*x), dy;
+    dy.data = y_local + static_cast<size_t>(b) * yel;
+    dy.rows = M;
+    dy.cols = w;
+    dy.ld = N;
+    dy.inner = 1;
+    PeerTargets peers;
+    for (int r = 0; r < g->n; ++r)
+      if (r != g->rank) peers.y[peers.n++] = g->base[r] + ybuf + static_cast<size_t>(b) * yel;
+    // TMA store maps over every rank's whole buffer (own first) when the
+    // row pitch is a multiple of 16 bytes; else per-thread stores.
+    YStoreMaps maps;
+    std::memset(&maps, 0, sizeof(maps));
+    if ((N * yel) % 16 == 0) {
+      maps.col0 = static_cast<int>(b);
+      if (encode_ystore_map(&maps.m[maps.n++], y_local, N, M, y_f32) != LLK_OK) return LLK_ERR_ALIGN;
+      for (int r = 0; r < g->n; ++r)
+        if (r != g->rank && encode_ystore_map(&maps.m[maps.n++], g->base[r] + ybuf, N, M, y_f32) != LLK_OK)
+          return LLK_ERR_ALIGN;
+      peers.maps = &maps;
+    }
+    bool fused = false;
+    {
+      std::lock_guard<std::mutex> lk(ds->mu);
+      rc = launch_device(*ds, LLK_OP_FUSED_SWIGLU, dx, dg, du, dy, y_f32, 0, requested, nullptr, 0, stream,
+                         &peers, &fused);
+    }
+    if (rc != LLK_OK) return rc;
+    if (!fused) {
+      // Kernels without the fused epilogue (small M): copy engines move
+      // this rank's columns to every peer over NVLink.
+      for (int i = 0; i < peers.n; ++i)
+        if (cudaMemcpy2DAsync(peers.y[i], static_cast<size_t>(N) * yel, dy.data, static_cast<size_t>(N) * yel,
+                              static_cast<size_t>(w) * yel, static_cast<size_t>(M), cudaMemcpyDeviceToDevice,
+                              stream) != cudaSuccess)
+          return LLK_ERR_CUDA;
+    }
+  }
+  peer_barrier_kernel<<<1, 32, 0, stream>>>(exit_, g->n, g->epoch, ds->status);
+  return cudaGetLastError() == cudaSuccess ? LLK_OK : LLK_ERR_CUDA;
 }
 
 }  // extern "C"

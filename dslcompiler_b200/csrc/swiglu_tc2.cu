@@ -55,6 +55,10 @@ constexpr uint32_t kSlabBytes = 64 * kBK * 2;       // 8 KB
 constexpr uint32_t kBBytes = 2 * kSlabBytes;        // 16 KB: this CTA's 128 columns
 constexpr uint32_t kStageBytes = kABytes + kBBytes;  // 32 KB
 constexpr uint32_t kTmemCols = 512;
+// Epilogue staging for TMA stores of Y: 8 KB per epilogue warp (4 chunks of
+// 32 x 32 bf16 or 2 of 32 x 32 f32), 1024-byte aligned after the stages.
+constexpr uint32_t kStagingPerWarp = 8192;
+constexpr uint32_t kStagingBytes = 4 * kStagingPerWarp;
 constexpr uint64_t kWaitLimitNs = 2000000000ull;
 
 // One unit of a pair's work: Y columns [c0, c0 + wn) of tile `tile`.
@@ -187,13 +191,15 @@ __device__ __forceinline__ bool next_work(const TcParams &p, PairTail *st, uint3
 template <int MODE>
 __global__ void __launch_bounds__(kThreads, 1)
     tc2_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__ CUtensorMap tm_b0,
-               const __grid_constant__ CUtensorMap tm_b1, const TcParams p) {
+               const __grid_constant__ CUtensorMap tm_b1, const TcParams p,
+               const __grid_constant__ YStoreMaps ym) {
   constexpr bool kSwiglu = (MODE == TC_SWIGLU_BF16 || MODE == TC_SWIGLU_F32);
   constexpr int kTileN = kSwiglu ? 128 : 256;
 
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  PairTail *st = reinterpret_cast<PairTail *>(smem + kStages * kStageBytes);
+  uint8_t *staging = smem + kStages * kStageBytes;
+  PairTail *st = reinterpret_cast<PairTail *>(staging + kStagingBytes);
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -356,6 +362,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int q = warp & 3;
     const int row_in_tile = q * 32 + lane;
     const uint32_t leader_tmem_empty = map_shared_rank(smem_u32(&st->tmem_empty[0]), 0);
+    uint32_t y_chunks = 0;  // chunks this warp staged for TMA stores
     Work w;
     bool ok = true;
     int posted = 0;
@@ -371,7 +378,56 @@ __global__ void __launch_bounds__(kThreads, 1)
       const int n0 = nt * kTileN + w.c0;
       const int row = m0 + row_in_tile;
       const uint32_t t_row = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + acc * kMmaN;
-      if (kSwiglu) {
+      if (kSwiglu && ym.n > 0) {
+        // Staged TMA stores: lane = row; the chunk goes to shared memory in
+        // the map's swizzled layout (64-byte rows for bf16, 128-byte for
+        // f32; the XOR keeps each 8-lane phase of the 16-byte stores on
+        // distinct banks), then one lane stores it through every map.
+        constexpr bool kBf16 = (MODE == TC_SWIGLU_BF16);
+        constexpr uint32_t kBuf = kBf16 ? 2048 : 4096;
+        constexpr int kNBuf = kStagingPerWarp / kBuf;
+        const uint32_t wstage = smem_u32(staging) + q * kStagingPerWarp;
+        const int r0 = m0 + q * 32;
+#pragma unroll 1
+        for (int c = 0; c < w.wn; c += 32) {
+          uint32_t g[32], u[32];
+          tmem_ld_32x32b_x32(t_row + c, g);
+          tmem_ld_32x32b_x32(t_row + w.wn + c, u);
+          tmem_ld_wait();
+          const int col = n0 + c;
+          if (r0 >= p.M || col >= p.N) continue;  // warp-uniform
+          float y[32];
+#pragma unroll
+          for (int j = 0; j < 32; ++j) y[j] = silu_mul(__uint_as_float(g[j]), __uint_as_float(u[j]));
+          const uint32_t buf = wstage + static_cast<uint32_t>(y_chunks % kNBuf) * kBuf;
+          if (lane == 0) bulk_wait_group_read<kNBuf - 1>();
+          __syncwarp();
+          if (kBf16) {
+            const uint32_t rowa = buf + lane * 64;
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+              const uint32_t phys = static_cast<uint32_t>(j) ^ ((lane >> 1) & 3u);
+              st_shared_v4(rowa + phys * 16, pack_bf16x2(y[8 * j], y[8 * j + 1]), pack_bf16x2(y[8 * j + 2], y[8 * j + 3]),
+                           pack_bf16x2(y[8 * j + 4], y[8 * j + 5]), pack_bf16x2(y[8 * j + 6], y[8 * j + 7]));
+            }
+          } else {
+            const uint32_t rowa = buf + lane * 128;
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+              const uint32_t phys = static_cast<uint32_t>(j) ^ (lane & 7u);
+              st_shared_v4(rowa + phys * 16, __float_as_uint(y[4 * j]), __float_as_uint(y[4 * j + 1]),
+                           __float_as_uint(y[4 * j + 2]), __float_as_uint(y[4 * j + 3]));
+            }
+          }
+          fence_proxy_async_smem();
+          __syncwarp();
+          if (lane == 0) {
+            for (int i = 0; i < ym.n; ++i) tma_store_2d(&ym.m[i], buf, ym.col0 + col, r0);
+            bulk_commit_group();
+          }
+          ++y_chunks;
+        }
+      } else if (kSwiglu) {
 #pragma unroll 1
         for (int c = 0; c < w.wn; c += 32) {
           uint32_t g[32], u[32];
@@ -383,29 +439,37 @@ __global__ void __launch_bounds__(kThreads, 1)
             float y[32];
 #pragma unroll
             for (int j = 0; j < 32; ++j) y[j] = silu_mul(__uint_as_float(g[j]), __uint_as_float(u[j]));
+            const int64_t off = (int64_t)row * p.ldy + col;
+            const bool vec = p.vec_ok && col + 32 <= p.N;
             if (MODE == TC_SWIGLU_BF16) {
-              uint16_t *dst = reinterpret_cast<uint16_t *>(p.y) + (int64_t)row * p.ldy + col;
-              if (p.vec_ok && col + 32 <= p.N) {
-                uint4 *d4 = reinterpret_cast<uint4 *>(dst);
+              uint32_t pk[16];
 #pragma unroll
-                for (int v = 0; v < 4; ++v)
-                  d4[v] = make_uint4(pack_bf16x2(y[8 * v + 0], y[8 * v + 1]), pack_bf16x2(y[8 * v + 2], y[8 * v + 3]),
-                                     pack_bf16x2(y[8 * v + 4], y[8 * v + 5]), pack_bf16x2(y[8 * v + 6], y[8 * v + 7]));
-              } else {
+              for (int j = 0; j < 16; ++j) pk[j] = pack_bf16x2(y[2 * j], y[2 * j + 1]);
+              // t = -1: this GPU's Y; t >= 0: the peers' (fused all-gather)
+              for (int t = -1; t < p.n_peers; ++t) {
+                uint16_t *dst = reinterpret_cast<uint16_t *>(t < 0 ? p.y : p.y_peers[t]) + off;
+                if (vec) {
+                  uint4 *d4 = reinterpret_cast<uint4 *>(dst);
 #pragma unroll
-                for (int j = 0; j < 32; ++j)
-                  if (col + j < p.N) dst[j] = static_cast<uint16_t>(pack_bf16x2(y[j], 0.f));
+                  for (int v = 0; v < 4; ++v) d4[v] = make_uint4(pk[4 * v], pk[4 * v + 1], pk[4 * v + 2], pk[4 * v + 3]);
+                } else {
+#pragma unroll
+                  for (int j = 0; j < 32; ++j)
+                    if (col + j < p.N) dst[j] = static_cast<uint16_t>(pk[j >> 1] >> ((j & 1) * 16));
+                }
               }
             } else {
-              float *dst = reinterpret_cast<float *>(p.y) + (int64_t)row * p.ldy + col;
-              if (p.vec_ok && col + 32 <= p.N) {
-                float4 *d4 = reinterpret_cast<float4 *>(dst);
+              for (int t = -1; t < p.n_peers; ++t) {
+                float *dst = reinterpret_cast<float *>(t < 0 ? p.y : p.y_peers[t]) + off;
+                if (vec) {
+                  float4 *d4 = reinterpret_cast<float4 *>(dst);
 #pragma unroll
-                for (int v = 0; v < 8; ++v) d4[v] = make_float4(y[4 * v], y[4 * v + 1], y[4 * v + 2], y[4 * v + 3]);
-              } else {
+                  for (int v = 0; v < 8; ++v) d4[v] = make_float4(y[4 * v], y[4 * v + 1], y[4 * v + 2], y[4 * v + 3]);
+                } else {
 #pragma unroll
-                for (int j = 0; j < 32; ++j)
-                  if (col + j < p.N) dst[j] = y[j];
+                  for (int j = 0; j < 32; ++j)
+                    if (col + j < p.N) dst[j] = y[j];
+                }
               }
             }
           }
@@ -418,8 +482,10 @@ __global__ void __launch_bounds__(kThreads, 1)
           tmem_ld_wait();
           const int col = n0 + c;
           if (row < p.M && col < p.N) {
-            float *dst = reinterpret_cast<float *>(p.y) + (int64_t)row * p.ldy + col;
-            if (p.vec_ok && col + 32 <= p.N) {
+            const int64_t off = (int64_t)row * p.ldy + col;
+            float *dst = reinterpret_cast<float *>(p.y) + off;
+            const bool vec = p.vec_ok && col + 32 <= p.N;
+            if (vec) {
               float4 *d4 = reinterpret_cast<float4 *>(dst);
 #pragma unroll
               for (int v = 0; v < 8; ++v) {
@@ -433,6 +499,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                   o.w += c4.w;
                 }
                 d4[v] = o;
+                for (int t = 0; t < p.n_peers; ++t) reinterpret_cast<float4 *>(reinterpret_cast<float *>(p.y_peers[t]) + off)[v] = o;
               }
             } else {
 #pragma unroll
@@ -441,6 +508,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                   float o = __uint_as_float(r[j]);
                   if (MODE == TC_MATMUL_F32_ACC) o += dst[j];
                   dst[j] = o;
+                  for (int t = 0; t < p.n_peers; ++t) reinterpret_cast<float *>(p.y_peers[t])[off + j] = o;
                 }
               }
             }
@@ -450,6 +518,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       tc_fence_before();
       mbar_arrive_cluster(leader_tmem_empty + acc * 8u);
     }
+    if (ym.n > 0 && lane == 0) bulk_wait_group_all();  // staging is read and the stores done before exit
   }
 
   tc_fence_before();
@@ -497,7 +566,8 @@ int resident_pairs() {
 
 template <int MODE>
 cudaError_t launch_pair_mode(const CUtensorMap &a, const CUtensorMap &b0, const CUtensorMap &b1, TcParams p,
-                             int max_pairs, int tail_split, int *sched_counter, cudaStream_t stream) {
+                             int max_pairs, int tail_split, int *sched_counter, cudaStream_t stream,
+                             const YStoreMaps &ym) {
   auto kern = tc2_kernel<MODE>;
   const int clusters = resident_pairs<MODE>();
   if (clusters < 1) return cudaErrorInvalidValue;
@@ -545,26 +615,30 @@ cudaError_t launch_pair_mode(const CUtensorMap &a, const CUtensorMap &b0, const 
   p.dynamic = sched_counter != nullptr ? 1 : 0;
   p.sched_counter = sched_counter;
   cfg.gridDim = dim3(2 * pairs);
-  e = cudaLaunchKernelEx(&cfg, kern, a, b0, b1, p);
+  e = cudaLaunchKernelEx(&cfg, kern, a, b0, b1, p, ym);
   if (e != cudaSuccess) return e;
   return cudaGetLastError();
 }
 
 }  // namespace
 
-int tc2_smem_bytes() { return kStages * kStageBytes + static_cast<int>(sizeof(PairTail)) + 1024; }
+int tc2_smem_bytes() { return kStages * kStageBytes + kStagingBytes + static_cast<int>(sizeof(PairTail)) + 1024; }
+static_assert(kStages * kStageBytes + kStagingBytes + sizeof(PairTail) + 1024 <= 227 * 1024,
+              "CTA-pair kernel shared memory over the 227 KB opt-in limit");
 
 cudaError_t tc2_launch(int mode, const CUtensorMap &a, const CUtensorMap &b0, const CUtensorMap &b1, TcParams p,
-                       int max_pairs, int tail_split, int *sched_counter, cudaStream_t stream) {
+                       int max_pairs, int tail_split, int *sched_counter, cudaStream_t stream, const YStoreMaps *ym) {
+  static const YStoreMaps kNoMaps = {};
+  const YStoreMaps &m = ym ? *ym : kNoMaps;
   switch (mode) {
     case TC_SWIGLU_BF16:
-      return launch_pair_mode<TC_SWIGLU_BF16>(a, b0, b1, p, max_pairs, tail_split, sched_counter, stream);
+      return launch_pair_mode<TC_SWIGLU_BF16>(a, b0, b1, p, max_pairs, tail_split, sched_counter, stream, m);
     case TC_SWIGLU_F32:
-      return launch_pair_mode<TC_SWIGLU_F32>(a, b0, b1, p, max_pairs, tail_split, sched_counter, stream);
+      return launch_pair_mode<TC_SWIGLU_F32>(a, b0, b1, p, max_pairs, tail_split, sched_counter, stream, m);
     case TC_MATMUL_F32:
-      return launch_pair_mode<TC_MATMUL_F32>(a, b0, b1, p, max_pairs, tail_split, sched_counter, stream);
+      return launch_pair_mode<TC_MATMUL_F32>(a, b0, b1, p, max_pairs, tail_split, sched_counter, stream, kNoMaps);
     case TC_MATMUL_F32_ACC:
-      return launch_pair_mode<TC_MATMUL_F32_ACC>(a, b0, b1, p, max_pairs, tail_split, sched_counter, stream);
+      return launch_pair_mode<TC_MATMUL_F32_ACC>(a, b0, b1, p, max_pairs, tail_split, sched_counter, stream, kNoMaps);
     default:
       return cudaErrorInvalidValue;
   }

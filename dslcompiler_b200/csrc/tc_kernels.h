@@ -39,6 +39,24 @@ struct TcParams {
   // group_m row blocks; inside a band the row block varies fastest, then the
   // column tile, so one band's X rows stay in L2 while the band sweeps N.
   int group_m;
+  // Column-parallel all-gather fused into the epilogue (CTA-pair kernel):
+  // every Y chunk is also stored at the same offsets from y_peers[0..n_peers)
+  // -- other GPUs' Y buffers mapped into this process -- so the shards
+  // travel over NVLink while later tiles compute.
+  int n_peers;
+  void *y_peers[7];
+};
+constexpr int kMaxYPeers = 7;
+
+// TMA store maps of the output (CTA-pair kernel): when n > 0 the SwiGLU
+// epilogue stages each 32 x 32 chunk in shared memory and stores it with
+// TMA through every map -- this GPU's Y and the peers' -- at column
+// col0 + (column in this launch's Y).  Maps: dims {N_full, M}, box {32, 32},
+// bf16 with 64-byte swizzle or f32 with 128-byte swizzle.
+struct YStoreMaps {
+  CUtensorMap m[kMaxYPeers + 1];
+  int n;
+  int col0;
 };
 
 int tc_smem_bytes();
@@ -48,8 +66,10 @@ int tc_smem_bytes();
 int tc2_smem_bytes();
 // sched_counter: a zeroed device int for the dynamic scheduler, or nullptr
 // for the static round-robin schedule.
+// ym: TMA store maps of Y (nullptr: per-thread stores to p.y / p.y_peers).
 cudaError_t tc2_launch(int mode, const CUtensorMap &a, const CUtensorMap &b0, const CUtensorMap &b1,
-                       TcParams p, int max_pairs, int tail_split, int *sched_counter, cudaStream_t stream);
+                       TcParams p, int max_pairs, int tail_split, int *sched_counter, cudaStream_t stream,
+                       const YStoreMaps *ym = nullptr);
 // Device bytes the dynamic scheduler needs (one zeroed int).
 constexpr size_t kTc2SchedBytes = 256;
 int tc_threads();

@@ -95,6 +95,93 @@ class ColumnShardedSwiGLU:
         return y
 
 
+class _DeviceArray:
+    """A raw device buffer seen through __cuda_array_interface__ (so torch
+    can view the library-owned group Y without copying)."""
+
+    def __init__(self, ptr: int, shape, typestr: str):
+        self.__cuda_array_interface__ = {"shape": tuple(shape), "typestr": typestr, "data": (ptr, False),
+                                         "version": 3, "strides": None}
+
+
+class PeerGroupSwiGLU:
+    """Column-parallel SwiGLU whose all-gather is fused into the kernel
+    (``llk_swiglu_column_parallel``): rank r computes its columns and the
+    epilogue stores them into every rank's Y over NVLink, so each call
+    leaves the whole Y[M, N] on every GPU with no collective launched.
+
+    wg, wu: this rank's [K, e-b] columns (``already_sharded=True``) or the
+    full [K, N] weights.  ``max_rows`` sizes the group Y buffer.  ``group``:
+    the torch.distributed group over which the IPC handles are exchanged
+    (any backend; gloo works).  One process per GPU, all ranks on one node.
+    """
+
+    def __init__(self, wg, wu, N: int, max_rows: int, *, out_dtype: str = "bf16", group=None,
+                 already_sharded: bool = False, pack: bool = True, device: int | None = None):
+        self.rank = dist.get_rank(group) if dist and dist.is_initialized() else 0
+        self.world = dist.get_world_size(group) if dist and dist.is_initialized() else 1
+        self.N, self.max_rows = N, max_rows
+        self.f32 = out_dtype in ("f32", "fp32", "float32")
+        self.begin, self.end = shard_columns(N, self.world, self.rank)
+        if not already_sharded:
+            wg = wg[:, self.begin:self.end]
+            wu = wu[:, self.begin:self.end]
+        self.device = device if device is not None else torch.cuda.current_device()
+        self._packed = PackedWeights(_contig(wg), _contig(wu), device=self.device) if pack else None
+        self.wg, self.wu = (None, None) if pack else (wg, wu)
+        h = ctypes.c_void_p()
+        buf = ctypes.create_string_buffer(capi.LLK_IPC_HANDLE_BYTES)
+        g = gpu_context(self.device, None)
+        el = 4 if self.f32 else 2
+        check(lib().llk_peer_group_create(self.world, self.rank, max_rows * N * el, ctypes.byref(g), ctypes.byref(h),
+                                          buf), "llk_peer_group_create")
+        self._h = h
+        mine = bytes(buf.raw)
+        if self.world > 1:
+            allh = [None] * self.world
+            dist.all_gather_object(allh, mine, group=group)
+        else:
+            allh = [mine]
+        check(lib().llk_peer_group_connect(self._h, b"".join(allh)), "llk_peer_group_connect")
+
+    def y(self, M: int):
+        """The Y [M, N] of the last call on this rank, as a torch tensor
+        viewing the library buffer (the group alternates two buffers: the
+        view stays valid until the call after next)."""
+        yp, yb = ctypes.c_void_p(), ctypes.c_int64()
+        check(lib().llk_peer_group_y(self._h, ctypes.byref(yp), ctypes.byref(yb)), "llk_peer_group_y")
+        arr = _DeviceArray(yp.value or 0, (M, self.N), "<f4" if self.f32 else "<i2")
+        t = torch.as_tensor(arr, device=torch.device("cuda", self.device))
+        return t if self.f32 else t.view(torch.bfloat16)
+
+    def __call__(self, x, *, stream=None):
+        """Y = SwiGLU(x, Wg, Wu) [M, N] on every rank (x replicated)."""
+        from .swiglu import tensor2d
+        M = x.shape[0]
+        if M > self.max_rows:
+            raise ValueError(f"M = {M} exceeds the group's max_rows = {self.max_rows}")
+        st = stream if stream is not None else torch.cuda.current_stream(self.device).cuda_stream
+        g = gpu_context(self.device, st, capi.LLK_DTYPE_FP32 if self.f32 else capi.LLK_DTYPE_BF16)
+        tx = tensor2d(x)
+        if self._packed is not None:
+            rc = lib().llk_swiglu_column_parallel(ctypes.byref(tx), None, None, self._packed._h, self.N, self._h,
+                                                  ctypes.byref(g))
+        else:
+            tg, tu = tensor2d(self.wg), tensor2d(self.wu)
+            rc = lib().llk_swiglu_column_parallel(ctypes.byref(tx), ctypes.byref(tg), ctypes.byref(tu), None, self.N,
+                                                  self._h, ctypes.byref(g))
+        check(rc, "llk_swiglu_column_parallel")
+        return self.y(M)
+
+    def close(self):
+        if getattr(self, "_h", None):
+            lib().llk_peer_group_destroy(self._h)
+            self._h = None
+        if self._packed is not None:
+            self._packed.close()
+            self._packed = None
+
+
 def gather_columns(gathered, bounds, y):
     """[world, M, width] shard-major -> row-major y[M, N].  CUDA tensors go
     through the library's kernel; CPU tensors (gloo test ranks) are copied
@@ -117,4 +204,4 @@ def _contig(w):
     return np.ascontiguousarray(w)
 
 
-__all__ = ["ColumnShardedSwiGLU", "gather_columns", "shard_bounds", "capi"]
+__all__ = ["ColumnShardedSwiGLU", "PeerGroupSwiGLU", "gather_columns", "shard_bounds", "capi"]

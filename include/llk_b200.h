@@ -257,6 +257,47 @@ int llk_shard_columns(int64_t N, int n_shards, int index, int64_t *begin, int64_
 int llk_gather_columns(const void *shards, int n_shards, int64_t M, int64_t width, const int64_t *begins, void *y,
                        int64_t ldy, int elem_bytes, const llk_gpu_context *gpu);
 
+/* ---- column-parallel SwiGLU with the all-gather fused in ----------------
+ * One process per GPU, n_ranks <= 8 on one node.  Each rank owns the
+ * columns llk_shard_columns(N, n_ranks, rank) of Wg/Wu and a replica of X;
+ * llk_swiglu_column_parallel computes those columns and the CTA-pair
+ * kernel's epilogue stores every finished chunk into EVERY rank's Y over
+ * NVLink (peer stores; the 1-CTA and decode kernels used for M <= 128 copy
+ * their columns with the copy engines instead), so when the call's work
+ * completes in stream order, this rank's group Y holds the whole Y[M, N]
+ * (row-major, row stride N, bf16 or f32 per gpu->y_dtype).  This replaces
+ * compute + ncclAllGather + relayout (the reference has no multi-device
+ * path).  Set-up, once per group:
+ *   1. every rank: llk_peer_group_create -> a handle of LLK_IPC_HANDLE_BYTES;
+ *   2. exchange the handles over any host channel (rank order);
+ *   3. every rank: llk_peer_group_connect with all n_ranks handles.
+ * Every rank must make the same sequence of calls.  Calls alternate
+ * between two Y buffers and end with a device-side barrier over the group
+ * (bounded: 2 s; a rank that never arrives makes the others report
+ * LLK_ERR_TIMEOUT through llk_synchronize), so a call never overwrites the
+ * buffer that a peer's stream may still be reading from the previous call.
+ * Consumers of a call's Y must run on the stream passed in gpu (or
+ * synchronise with it) and finish before the call after next. */
+#define LLK_IPC_HANDLE_BYTES 64
+typedef struct llk_peer_group llk_peer_group;
+
+/* y_bytes: capacity of one Y buffer (>= M * N * element size of any call;
+ * the group holds two). */
+int llk_peer_group_create(int n_ranks, int rank, int64_t y_bytes, const llk_gpu_context *gpu, llk_peer_group **out,
+                          unsigned char *ipc_handle);
+/* all_handles: n_ranks * LLK_IPC_HANDLE_BYTES bytes, rank r's at r * 64. */
+int llk_peer_group_connect(llk_peer_group *g, const unsigned char *all_handles);
+/* The Y buffer (device) the last call wrote on this rank, and its capacity. */
+int llk_peer_group_y(const llk_peer_group *g, void **y, int64_t *bytes);
+void llk_peer_group_destroy(llk_peer_group *g);
+/* x: device X [M, K]; this rank's weight columns as device Tensor2D pair
+ * (wg_shard, wu_shard: [K, e - b]) or as packed weights (pw_shard, then
+ * wg_shard / wu_shard are ignored); N = full width.  Asynchronous on
+ * gpu->stream. */
+int llk_swiglu_column_parallel(const Tensor2D *x, const Tensor2D *wg_shard, const Tensor2D *wu_shard,
+                               const llk_packed_weights *pw_shard, int64_t N, llk_peer_group *g,
+                               const llk_gpu_context *gpu);
+
 /* ---- target probe (analogue of lib/Target/X86/TargetAVX2.cpp:33-92) ---- */
 
 typedef struct llk_cuda_target {
