@@ -586,12 +586,16 @@ cudaError_t launch_pair_mode(const CUtensorMap &a, const CUtensorMap &b0, const 
   int pairs = clusters;
   if (max_pairs >= 1 && pairs > max_pairs) pairs = max_pairs;
   // Whole-tile waves, then the leftover tiles cut into g column parts.  A
-  // part still loads its tile's whole X block (16 KB per CTA per k-block)
-  // but only 1/g of the weight bytes (16 KB / g), and the k-loop is bound by
-  // these L2->shared-memory bytes (measured: a quarter part takes ~0.63 of a
-  // whole tile), so a part costs (1 + 1/g) / 2 tile-times.  The last wave
+  // part of width 256/g does not take 1/g of a tile: its k-blocks keep a
+  // cost that does not shrink with the MMA's N (it still loads the tile's
+  // whole X block; measured on B200: a quarter part takes ~0.63 of a whole
+  // tile), so a part is charged (1 + 1/g) / 2 tile-times.  The last wave
   // then takes ceil(left * g / pairs) * (1 + 1/g) / 2; pick the g that
-  // makes it shortest (ties: the wider tiles).
+  // makes it shortest (ties: the wider tiles).  Cutting along K instead
+  // (partial sums through L2, ordered fix-up by the last part) was built
+  // and measured slower on every shape tried (8-GPU config-3 shard: 93 us
+  // against 50 us): re-reading 128 KB of f32 rows per part costs more than
+  // the shorter wave saves.
   p.group_m = kBandBlocks < p.m_tiles ? kBandBlocks : p.m_tiles;
   p.dp_waves = p.num_tiles / pairs;
   const int left = p.num_tiles - p.dp_waves * pairs;
