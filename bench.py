@@ -367,16 +367,19 @@ def our_arm(args):
     extras = {}
     n_sets = len(sets)
     if world > 1:
-        extras["gather_y"] = gather_timing(args, dev, stream, yd, N, world, barrier, max_over_ranks)
-        extras["fused_allgather"] = fused_allgather_timing(args, dev, stream, xd, gd, ud, N, barrier, max_over_ranks,
-                                                           job_ms, extras["gather_y"]["ms"])
+        extras["gather_y"] = secondary(lambda: gather_timing(args, dev, stream, yd, N, world, barrier, max_over_ranks))
+        if "error" not in extras["gather_y"]:
+            extras["fused_allgather"] = secondary(lambda: fused_allgather_timing(
+                args, dev, stream, xd, gd, ud, N, barrier, max_over_ranks, job_ms, extras["gather_y"]["ms"]))
     cpu = None
     if not args.quick:
         del sets, xd, gd, ud, yd
         torch.cuda.empty_cache()
-        extras.update(sharded_extras(args, dev, stream, rank, world, peak_tf, peak_gbs, barrier, max_over_ranks))
+        extras.update(secondary(lambda: sharded_extras(args, dev, stream, rank, world, peak_tf, peak_gbs, barrier,
+                                                       max_over_ranks), "sharded_extras"))
         if world == 1:
-            extras.update(single_gpu_extras(args, dev, stream, peak_tf, peak_gbs))
+            extras.update(secondary(lambda: single_gpu_extras(args, dev, stream, peak_tf, peak_gbs),
+                                    "single_gpu_extras"))
             if not args.no_cpu_baseline:
                 cpu = cpu_baseline(x, wg, wu)
 
@@ -445,6 +448,21 @@ def gather_timing(args, dev, stream, yd, N, world, barrier, max_over_ranks):
     recv = (world - 1) * M * width * yd.element_size()
     return {"ms": ms, "bytes_received_per_gpu": recv, "GB/s_per_gpu": recv / (ms * 1e-3) / 1e9,
             "what": "all_gather_into_tensor (NCCL) of padded Y shards + llk_gather_columns relayout"}
+
+
+def secondary(fn, key=None):
+    """Runs a secondary measurement; an exception is reported in the JSON
+    line (under `key` when given) instead of ending the run, so the headline
+    line is always printed.  Every rank runs the same measurements, so they
+    fail alike and no rank is left waiting in a collective."""
+    try:
+        return fn()
+    except Exception as e:  # noqa: BLE001
+        import traceback
+
+        traceback.print_exc(file=sys.stderr)
+        err = {"error": f"{type(e).__name__}: {e}"[:300]}
+        return {key: err} if key else err
 
 
 def fused_allgather_timing(args, dev, stream, xd, gd, ud, N, barrier, max_over_ranks, kernel_ms, gather_ms):
