@@ -118,6 +118,7 @@ class PeerGroupSwiGLU:
 
     def __init__(self, wg, wu, N: int, max_rows: int, *, out_dtype: str = "bf16", group=None,
                  already_sharded: bool = False, pack: bool = True, device: int | None = None):
+        self.group = group
         self.rank = dist.get_rank(group) if dist and dist.is_initialized() else 0
         self.world = dist.get_world_size(group) if dist and dist.is_initialized() else 1
         self.N, self.max_rows = N, max_rows
@@ -174,7 +175,12 @@ class PeerGroupSwiGLU:
         return self.y(M)
 
     def close(self):
+        """Frees the group on every rank: collective (all ranks call it), so
+        no peer is still storing into this rank's buffers when they go."""
         if getattr(self, "_h", None):
+            torch.cuda.synchronize(self.device)
+            if self.world > 1 and dist is not None and dist.is_initialized():
+                dist.barrier(group=self.group)
             lib().llk_peer_group_destroy(self._h)
             self._h = None
         if self._packed is not None:

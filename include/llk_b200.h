@@ -289,6 +289,11 @@ int llk_peer_group_create(int n_ranks, int rank, int64_t y_bytes, const llk_gpu_
 int llk_peer_group_connect(llk_peer_group *g, const unsigned char *all_handles);
 /* The Y buffer (device) the last call wrote on this rank, and its capacity. */
 int llk_peer_group_y(const llk_peer_group *g, void **y, int64_t *bytes);
+/* Unmaps the peers and frees this rank's buffers.  Every rank's work on the
+ * group must be finished first (e.g. synchronise the streams, then a host
+ * barrier across ranks): a peer's kernel may still store into this rank's
+ * buffers until its call completes.  A group is used by one host thread at
+ * a time. */
 void llk_peer_group_destroy(llk_peer_group *g);
 /* x: device X [M, K]; this rank's weight columns as device Tensor2D pair
  * (wg_shard, wu_shard: [K, e - b]) or as packed weights (pw_shard, then
