@@ -185,3 +185,23 @@ def test_llk_bench_and_tune_on_gpu(tmp_path):
     assert r.returncode == 0, r.stderr
     ents = schedule.read_db(str(out))
     assert len(ents) == 3 and all(e.measured_gflops > 0 for e in ents)
+
+
+def test_micro_perf_clock_override_and_measured(tmp_path):
+    """--clock-hz rescales the matrix-engine bound and keeps DRAM's bytes per
+    second; --measured-us reports predicted / measured."""
+    out = tmp_path / "c4.micro.mlir"
+    src = os.path.join(ROOT, "dslcompiler_b200", "examples", "llk", "c4_m1.mlir")
+    assert _run(["dslcompiler_b200.cli.llk_compile", src, "--emit", "micro", "-o", str(out)]).returncode == 0
+    a = yaml.safe_load(_run(["dslcompiler_b200.cli.micro_perf", str(out)]).stdout)
+    b = yaml.safe_load(_run(["dslcompiler_b200.cli.micro_perf", str(out), "--clock-hz", "1e9",
+                             "--measured-us", "40"]).stdout)
+    assert a["bottleneck"] == "dram_bandwidth" == b["bottleneck"]
+    assert abs(a["predicted_ns"] - b["predicted_ns"]) < 0.01 * a["predicted_ns"]  # DRAM time: clock-independent
+    assert b["measured_us"] == 40 and abs(b["efficiency"] - b["predicted_ns"] / 40e3) < 1e-3
+    c3 = tmp_path / "c3.micro.mlir"
+    src = os.path.join(ROOT, "dslcompiler_b200", "examples", "llk", "c3.mlir")
+    assert _run(["dslcompiler_b200.cli.llk_compile", src, "--emit", "micro", "-o", str(c3)]).returncode == 0
+    f = yaml.safe_load(_run(["dslcompiler_b200.cli.micro_perf", str(c3)]).stdout)
+    s = yaml.safe_load(_run(["dslcompiler_b200.cli.micro_perf", str(c3), "--clock-hz", "982500000"]).stdout)
+    assert f["bottleneck"] == "matrix_engine" and abs(s["predicted_ns"] / f["predicted_ns"] - 2.0) < 0.01
