@@ -145,6 +145,30 @@ def cpu_baseline(x, wg, wu, budget_s=12.0):
                       f"(~{sum(times) + t:.0f} s); oracle/swiglu_port.c fused schedule BM=32 BN=64 BK=64"}
 
 
+def reference_naive_baseline():
+    """The reference's own naive f32 swiglu_reference (its test oracle,
+    compiled from the reference's sources into oracle/_ref/ref_driver when
+    the reference tree was present at build time), one thread, on configs 1
+    and 4 (M = 1): what the reference runs on the CPU for this op.  None when
+    the binary is absent."""
+    exe = os.path.join(ROOT, "oracle", "_ref", "ref_driver")
+    if not os.access(exe, os.X_OK):
+        return None
+    out = {}
+    for name, (M, N, K, reps) in {"c1": (64, 512, 256, 5), "c4_m1": (1, 14336, 4096, 2)}.items():
+        try:
+            r = subprocess.run([exe, "time", str(M), str(N), str(K), str(reps)], capture_output=True, text=True,
+                               timeout=120)
+            sec = float(r.stdout.split()[0])
+        except Exception as e:  # noqa: BLE001
+            out[name] = {"error": str(e)[:200]}
+            continue
+        out[name] = {"gflops": 4.0 * M * N * K / sec / 1e9, "ms": sec * 1e3, "threads": 1,
+                     "shape": f"M={M} N={N} K={K}"}
+    return {"kind": "reference", "what": "test/Execution/swiglu_reference.cpp swiglu_reference (naive f32 loops)",
+            "configs": out}
+
+
 def reference_arm(args):
     rank, _, world = dist_env()
     if rank != 0:
@@ -382,6 +406,9 @@ def our_arm(args):
                                     "single_gpu_extras"))
             if not args.no_cpu_baseline:
                 cpu = cpu_baseline(x, wg, wu)
+                naive = secondary(reference_naive_baseline)
+                if naive:
+                    cpu["reference_naive"] = naive
 
     clocks = sampler.summary() if sampler else None
     if rank == 0:

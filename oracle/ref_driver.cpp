@@ -12,9 +12,14 @@
 //   ref_driver swiglu M N K x wg wu y32 y64 read f32 inputs (raw little-
 //                                           endian files), write the
 //                                           reference's f32 and f64 outputs
+//   ref_driver time M N K reps              time the reference's naive f32
+//                                           swiglu_reference (one thread) on
+//                                           seeded inputs: prints the best
+//                                           seconds per call
 #include "test/Execution/swiglu_reference.cpp"
 
 #include <cstdio>
+#include <chrono>
 #include <cstdlib>
 #include <string>
 
@@ -64,8 +69,32 @@ int main(int argc, char **argv) {
     }
     return 0;
   }
+  if (argc == 6 && std::string(argv[1]) == "time") {
+    int64_t M = std::atoll(argv[2]), N = std::atoll(argv[3]),
+            K = std::atoll(argv[4]);
+    const int reps = std::atoi(argv[5]);
+    if (M <= 0 || N <= 0 || K <= 0 || reps <= 0) return 1;
+    std::vector<float> x(M * K), wg(K * N), wu(K * N), y(M * N);
+    uint32_t st = 12345u;  // LCG in [-1, 1): the timing does not depend on values
+    auto rnd = [&st]() {
+      st = st * 1664525u + 1013904223u;
+      return static_cast<float>(st >> 8) / 8388608.0f - 1.0f;
+    };
+    for (auto &v : x) v = rnd();
+    for (auto &v : wg) v = rnd() * 0.02f;
+    for (auto &v : wu) v = rnd() * 0.02f;
+    double best = 1e30;
+    for (int r = 0; r < reps; ++r) {
+      auto t0 = std::chrono::steady_clock::now();
+      swiglu_reference(x.data(), wg.data(), wu.data(), y.data(), M, N, K);
+      double dt = std::chrono::duration<double>(std::chrono::steady_clock::now() - t0).count();
+      if (dt < best) best = dt;
+    }
+    std::printf("%.9f %g\n", best, static_cast<double>(y[0]));
+    return 0;
+  }
   std::fprintf(stderr,
                "usage: ref_driver gtest | ref_driver swiglu M N K x wg wu "
-               "y32 y64\n");
+               "y32 y64 | ref_driver time M N K reps\n");
   return 1;
 }
