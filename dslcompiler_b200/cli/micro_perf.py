@@ -7,7 +7,7 @@ import argparse
 import os
 import sys
 
-from .. import microperf
+from .. import compiler, microperf
 
 DEFAULT_MACHINE = os.path.join(os.path.dirname(os.path.dirname(os.path.abspath(__file__))), "machines",
                                "b200-sm100a.yaml")
@@ -41,7 +41,13 @@ def main(argv=None) -> int:
             m["bandwidth_bytes_per_cycle"] = float(m["bandwidth_bytes_per_cycle"]) * machine.clock_hz / a.clock_hz
             machine.memory = dict(machine.memory, dram=m)
         machine.clock_hz = a.clock_hz
-    rep = microperf.l0_bound(open(a.input).read(), machine)
+    text = open(a.input).read()
+    errs = compiler.verify_micro(text)
+    if errs:
+        for e in errs:
+            print(f"error: {a.input}: {e}", file=sys.stderr)
+        return 1
+    rep = microperf.l0_bound(text, machine)
     ns = rep.predicted_cycles / machine.clock_hz * 1e9
     if a.format == "yaml":
         text = microperf.report_yaml(rep, machine)

@@ -163,6 +163,74 @@ def _plan(op: str, M: int, N: int, K: int, y_dtype: str, variant: str = "auto") 
     return key.plan(M)
 
 
+_DEF_RE = re.compile(r"^\s*(%\w+)(?:\s*,\s*%\w+)?\s*=\s*micro\.(\w+)\b(.*)$")
+_ALLOC_TYPE_RE = re.compile(r"micro\.(?:alloc|tile_alloc)\s+tensor<([^>]*)>")
+_TRAILING_TYPE_RE = re.compile(r":\s*tensor<([^>]*)>\s*$")
+_MMA_LINE_RE = re.compile(r"micro\.mma\s+(%\w+)\s*,\s*(%\w+)\s*,\s*(%\w+)\s*\{(.*)\}")
+_SHAPE_ATTR_RE = re.compile(r"shape\s*=\s*\[([^\]]*)\]")
+_DTYPE_ATTR_RE = re.compile(r"(input|accumulator)\s*=\s*#micro\.dtype<(\w+)>")
+
+
+def _tensor(spec: str):
+    parts = spec.split("x")
+    return [int(d) if d != "?" else -1 for d in parts[:-1]], parts[-1].strip()
+
+
+def verify_micro(text: str) -> list[str]:
+    """The micro.mma verifier rules (``lib/Dialect/Micro/MicroOps.cpp:246-291``)
+    over micro IR text: each mma's operand types come from the ops that
+    define them.  Returns the error messages (empty: valid)."""
+    types = {}
+    errors = []
+    for n, line in enumerate(text.splitlines(), 1):
+        m = _DEF_RE.match(line)
+        if m:
+            t = _ALLOC_TYPE_RE.search(line) or _TRAILING_TYPE_RE.search(line)
+            if t:
+                types[m.group(1)] = _tensor(t.group(1))
+        mm = _MMA_LINE_RE.search(line)
+        if not mm:
+            continue
+
+        def err(msg):
+            errors.append(f"line {n}: 'micro.mma' op {msg}")
+
+        operands = [types.get(v) for v in mm.group(1, 2, 3)]
+        if any(o is None for o in operands):
+            err("mma operands and result must be tile types")
+            continue
+        sh = _SHAPE_ATTR_RE.search(mm.group(4))
+        shape = [int(v) for v in sh.group(1).split(",")] if sh and sh.group(1).strip() else []
+        if len(shape) != 3:
+            err("mma shape must have exactly 3 dimensions")
+            continue
+        if any(d <= 0 for d in shape):
+            err("mma shape dimensions must be positive")
+            continue
+        M_, N_, K_ = shape
+        (ls, lt), (rs, rt), (as_, at) = operands
+        if len(ls) != 2 or len(rs) != 2 or len(as_) != 2:
+            err("mma operands and result must be rank-2 tiles")
+            continue
+
+        def fits(expected, actual):
+            return actual == -1 or expected == actual
+
+        if not (fits(M_, ls[0]) and fits(K_, ls[1])):
+            err("lhs tile shape must be [M, K]")
+        elif not (fits(K_, rs[0]) and fits(N_, rs[1])):
+            err("rhs tile shape must be [K, N]")
+        elif not (fits(M_, as_[0]) and fits(N_, as_[1])):
+            err("accumulator tile shape must be [M, N]")
+        else:
+            dts = dict(_DTYPE_ATTR_RE.findall(mm.group(4)))
+            if lt != dts.get("input") or rt != dts.get("input"):
+                err("input dtype must match operand element types")
+            elif at != dts.get("accumulator"):
+                err("accumulator dtype must match accumulator element type")
+    return errors
+
+
 def lower_to_micro(op: LLKOp, M: int, N: int, K: int, variant: str = "auto", schedule_id: str = "") -> Lowered:
     """The micro.kernel for the kernel and plan that will run this op."""
     y_dtype = op.result_type.dtype if op.result_type.dtype in ("bf16", "f32") else "bf16"
@@ -213,26 +281,32 @@ def lower_to_micro(op: LLKOp, M: int, N: int, K: int, variant: str = "auto", sch
         L.append("    }")
         L.append("  }")
     else:  # decode kernel: weight-streaming, Y^T = W^T X^T, stream-K over (tile, k-block)
+        # W^T and X^T are column-major views of the row-major W and X, so
+        # each micro.mma is [M, K] x [K, N] -> [M, N] with M = 128 weight
+        # columns and N = the padded token count; gate and up accumulate in
+        # two accumulators (adjacent TMEM columns on the device).
         mp, bk = plan["block_m"], plan["block_k"]
         L.append(f'micro.kernel @{name} attributes {{workload = "{op.op}", target = "b200-sm100a", '
                  f'candidate = "decode_kernel", schedule_id = "{sid}", grid = {plan["grid"]}}} {{')
         L.append(f"  micro.spatial_for %bn = 0 to {N} step 128 map = #micro.map<worker> {{")
-        L.append(f"    %acc = micro.alloc tensor<128x{2 * mp}xf32> memory = #micro.memory<acc>")
+        for w in ["wg", "wu"]:
+            L.append(f"    %acc_{w} = micro.alloc tensor<128x{mp}xf32> memory = #micro.memory<acc>")
         L.append(f"    micro.pipeline stages = {plan['stages']} {{")
         L.append(f"      micro.for %bk = 0 to {K} step {bk} {{")
         for i, w in enumerate(["wg", "wu"]):
-            L.append(f"        %{w}_view = micro.tile_view %arg{i + 1}[%bk, %bn] {{shape = [{bk}, 128], layout = #micro.layout<row_major>}}")
-            L.append(f"        %{w}, %{w}_tok = micro.async_copy %{w}_view {{src_memory = #micro.memory<dram>, dst_memory = #micro.memory<sram>, owner = #micro.owner<dma>, layout = \"swizzled_128b\"}} : tensor<{bk}x128xbf16>")
-        L.append(f"        %x_view = micro.tile_view %arg0[0, %bk] {{shape = [{mp}, {bk}], layout = #micro.layout<row_major>}}")
-        L.append(f"        %x, %x_tok = micro.async_copy %x_view {{src_memory = #micro.memory<l2>, dst_memory = #micro.memory<sram>, owner = #micro.owner<dma>}} : tensor<{mp}x{bk}xbf16>")
+            L.append(f"        %{w}_view = micro.tile_view %arg{i + 1}[%bk, %bn] {{shape = [128, {bk}], layout = #micro.layout<col_major>}}")
+            L.append(f"        %{w}, %{w}_tok = micro.async_copy %{w}_view {{src_memory = #micro.memory<dram>, dst_memory = #micro.memory<sram>, owner = #micro.owner<dma>, layout = \"swizzled_128b\"}} : tensor<128x{bk}xbf16>")
+        L.append(f"        %x_view = micro.tile_view %arg0[0, %bk] {{shape = [{bk}, {mp}], layout = #micro.layout<col_major>}}")
+        L.append(f"        %x, %x_tok = micro.async_copy %x_view {{src_memory = #micro.memory<l2>, dst_memory = #micro.memory<sram>, owner = #micro.owner<dma>}} : tensor<{bk}x{mp}xbf16>")
         L.append("        micro.wait %wg_tok, %wu_tok, %x_tok")
         for w in ["wg", "wu"]:
-            L.append(f"        micro.mma %{w}, %x, %acc {{shape = [128, {mp}, {bk}], input = #micro.dtype<bf16>, "
+            L.append(f"        micro.mma %{w}, %x, %acc_{w} {{shape = [128, {mp}, {bk}], input = #micro.dtype<bf16>, "
                      f"accumulator = #micro.dtype<f32>, engine = \"tcgen05.cta_group::1\", owner = #micro.owner<matrix_engine>}}")
         L.append("      }")
         L.append("    }")
-        L.append('    %silu = micro.vector "silu" %acc {math_mode = "strict"}')
-        L.append(f"    micro.store %silu, %arg3 {{src_memory = #micro.memory<acc>, dst_memory = #micro.memory<dram>}} : tensor<{mp}x128x{y_dtype}>")
+        L.append('    %silu = micro.vector "silu" %acc_wg {math_mode = "strict"}')
+        L.append('    %out = micro.vector "mul" %silu, %acc_wu')
+        L.append(f"    micro.store %out, %arg3 {{src_memory = #micro.memory<acc>, dst_memory = #micro.memory<dram>}} : tensor<{mp}x128x{y_dtype}>")
         L.append("  }")
     L.append("  micro.yield")
     L.append("}")

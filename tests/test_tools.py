@@ -205,3 +205,41 @@ def test_micro_perf_clock_override_and_measured(tmp_path):
     f = yaml.safe_load(_run(["dslcompiler_b200.cli.micro_perf", str(c3)]).stdout)
     s = yaml.safe_load(_run(["dslcompiler_b200.cli.micro_perf", str(c3), "--clock-hz", "982500000"]).stdout)
     assert f["bottleneck"] == "matrix_engine" and abs(s["predicted_ns"] / f["predicted_ns"] - 2.0) < 0.01
+
+
+@pytest.mark.parametrize("M,variant", [(2048, "auto"), (64, "auto"), (1, "auto"), (16, "decode"), (100, "tc")])
+def test_lowered_micro_passes_the_mma_verifier(M, variant):
+    ops = compiler.parse_llk(SWIGLU.format(M=M, K=4096, N=11008, N2=11008))
+    low = compiler.lower_to_micro(ops[0], M, 11008, 4096, variant=variant)
+    assert compiler.verify_micro(low.text) == []
+    mm = compiler.parse_llk(MATMUL)
+    assert compiler.verify_micro(compiler.lower_to_micro(mm[0], 4096, 4096, 4096).text) == []
+
+
+def test_micro_mma_verifier_messages(tmp_path):
+    """The rules and messages of MicroOps.cpp:246-291 for micro.mma."""
+    base = ("%a, %t0 = micro.async_copy %v {{}} : tensor<{a}>\n"
+            "%b, %t1 = micro.async_copy %w {{}} : tensor<{b}>\n"
+            "%c = micro.alloc tensor<{c}> memory = #micro.memory<acc>\n"
+            "micro.mma %a, %b, %c {{shape = [{s}], input = #micro.dtype<bf16>, accumulator = #micro.dtype<f32>}}\n")
+    ok = dict(a="128x64xbf16", b="64x256xbf16", c="128x256xf32", s="128, 256, 64")
+    assert compiler.verify_micro(base.format(**ok)) == []
+    cases = {
+        "mma shape must have exactly 3 dimensions": dict(ok, s="128, 256"),
+        "mma shape dimensions must be positive": dict(ok, s="128, 0, 64"),
+        "lhs tile shape must be [M, K]": dict(ok, a="64x128xbf16"),
+        "rhs tile shape must be [K, N]": dict(ok, b="256x64xbf16"),
+        "accumulator tile shape must be [M, N]": dict(ok, c="128x128xf32"),
+        "input dtype must match operand element types": dict(ok, b="64x256xf16"),
+        "accumulator dtype must match accumulator element type": dict(ok, c="128x256xbf16"),
+        "mma operands and result must be rank-2 tiles": dict(ok, a="128x64x2xbf16"),
+    }
+    for msg, kw in cases.items():
+        errs = compiler.verify_micro(base.format(**kw))
+        assert len(errs) == 1 and errs[0].endswith(msg), (msg, errs)
+    assert compiler.verify_micro("micro.mma %p, %q, %r {shape = [1, 1, 1]}")[0].endswith(
+        "mma operands and result must be tile types")
+    bad = tmp_path / "bad.micro.mlir"
+    bad.write_text(base.format(**dict(ok, a="64x128xbf16")))
+    r = _run(["dslcompiler_b200.cli.micro_perf", str(bad)])
+    assert r.returncode == 1 and "lhs tile shape must be [M, K]" in r.stderr
