@@ -529,3 +529,26 @@ def test_packed_weights_l4_cache():
     b.close()
     llk.cache_level_set_max_entries(4, 64)
     llk.cache_level_clear(4)
+
+
+def test_fused_call_allocates_no_intermediate():
+    """The fused kernel keeps gate and up in TMEM: after the first call (the
+    library's workspace and plan), further calls of config-3 size allocate no
+    device memory at all -- in particular no [M, N] intermediate (the
+    reference checks the same of its fused IR, test/Execution/
+    swiglu_fused_memory.cpp:152-183)."""
+    M, K, N = 2048, 4096, 11008
+    x = torch.randn(M, K, device="cuda").bfloat16()
+    wg = (torch.randn(K, N, device="cuda") * 0.02).bfloat16()
+    wu = (torch.randn(K, N, device="cuda") * 0.02).bfloat16()
+    y = torch.empty(M, N, device="cuda", dtype=torch.bfloat16)
+    for _ in range(2):
+        llk.fused_swiglu(x, wg, wu, out=y)
+    torch.cuda.synchronize()
+    free0, _ = torch.cuda.mem_get_info()
+    for _ in range(20):
+        llk.fused_swiglu(x, wg, wu, out=y)
+    torch.cuda.synchronize()
+    llk.synchronize(0)
+    free1, _ = torch.cuda.mem_get_info()
+    assert free1 == free0, (free0 - free1)
