@@ -138,12 +138,17 @@ class PeerGroupSwiGLU:
                                           buf), "llk_peer_group_create")
         self._h = h
         mine = bytes(buf.raw)
-        if self.world > 1:
-            allh = [None] * self.world
-            dist.all_gather_object(allh, mine, group=group)
-        else:
-            allh = [mine]
-        check(lib().llk_peer_group_connect(self._h, b"".join(allh)), "llk_peer_group_connect")
+        try:
+            if self.world > 1:
+                allh = [None] * self.world
+                dist.all_gather_object(allh, mine, group=group)
+            else:
+                allh = [mine]
+            check(lib().llk_peer_group_connect(self._h, b"".join(allh)), "llk_peer_group_connect")
+        except Exception:
+            lib().llk_peer_group_destroy(self._h)
+            self._h = None
+            raise
 
     def y(self, M: int):
         """The Y [M, N] of the last call on this rank, as a torch tensor
