@@ -46,75 +46,131 @@ def dist_env():
 
 
 def measured_peaks():
-    """(bf16 TFLOP/s, HBM GB/s, source).  The bf16 figure is the SUSTAINED
-    one: the timed loop runs back to back for a sizeable fraction of a
-    second, long enough for the 1 kW power cap to set the clock, which is the
-    regime of the seconds-long cuBLAS loop the sustained figure measures."""
+    """{"burst", "sustained", "hbm", "source"} from MEASURED_PEAKS.json: bf16
+    TFLOP/s of a cuBLAS GEMM timed alone (burst) and held for seconds under
+    the power cap (sustained), and the HBM copy bandwidth in GB/s.  Without
+    the file, the pool's earlier measurement (1590 / 1400 TFLOP/s, 6650 GB/s)."""
     p = os.path.join(ROOT, "MEASURED_PEAKS.json")
     if os.path.exists(p):
         with open(p) as f:
             d = json.load(f)
-        return d.get("bf16_tflops_sustained") or d.get("bf16_tflops"), d.get("hbm_gbs"), "measured"
-    return 1400.0, 6650.0, "fallback"
+        burst = d.get("bf16_tflops") or d.get("bf16_tflops_sustained")
+        return {"burst": burst, "sustained": d.get("bf16_tflops_sustained") or burst, "hbm": d.get("hbm_gbs"),
+                "source": "measured"}
+    return {"burst": 1590.0, "sustained": 1400.0, "hbm": 6650.0, "source": "fallback"}
 
 
-def profile_traffic(name):
-    """dram bytes per launch recorded from an ncu capture in profiles/<name>.md
-    (a line 'traffic_bytes_per_launch: <int>')."""
-    p = os.path.join(ROOT, "profiles", name + ".md")
+def choose_peak(peaks, region_s, clocks):
+    """The bf16 denominator for a timed region: the sustained figure only when
+    the region ran long enough to reach the power cap (over one second) AND
+    its own clock samples show sw_power_cap; the burst figure otherwise."""
+    capped = bool(clocks) and "sw_power_cap" in (clocks.get("reasons") or [])
+    if region_s > 1.0 and capped:
+        return peaks["sustained"], "sustained", f"region {region_s:.3f} s with sw_power_cap in its clock samples"
+    why = "no sw_power_cap in its clock samples" if not capped else "shorter than 1 s"
+    return peaks["burst"], "burst", f"region {region_s:.3f} s, {why}"
+
+
+def profile_traffic(kernel, shard_cols):
+    """DRAM bytes (read + write) per launch of `kernel` on a shard of
+    `shard_cols` columns, from the machine-readable ncu summary
+    profiles/<kernel>.json ({"launches": [{"N": .., "dram_bytes": ..}, ..]});
+    None when no capture of that width is recorded."""
+    p = os.path.join(ROOT, "profiles", kernel + ".json")
     if not os.path.exists(p):
         return None
-    m = re.search(r"traffic_bytes_per_launch:\s*([0-9.eE+]+)", open(p).read())
-    return float(m.group(1)) if m else None
+    with open(p) as f:
+        d = json.load(f)
+    for e in d.get("launches", []):
+        if int(e.get("N", -1)) == int(shard_cols):
+            return {"bytes": float(e["dram_bytes"]), "source": f"profiles/{kernel}.json ({e.get('what', '')})"}
+    return None
 
 
 class ClockSampler:
-    """nvidia-smi clocks / throttle reasons sampled while the timed region runs."""
-    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,clocks_event_reasons.hw_slowdown,"
-         "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
-         "clocks_event_reasons.sw_power_cap")
+    """SM clock, power and clock-event (throttle) reasons of the given CUDA
+    devices, polled through NVML every few milliseconds from a background
+    thread, each sample time-stamped so that the samples inside the timed
+    region can be told from those of the warm-up around it."""
 
-    def __init__(self, gpus):
-        self.gpus = set(gpus)
-        self.rows = []
-        self.proc = None
+    REASONS = {0x4: "sw_power_cap", 0x8: "hw_slowdown", 0x20: "sw_thermal_slowdown", 0x40: "hw_thermal_slowdown",
+               0x80: "hw_power_brake_slowdown"}
+
+    def __init__(self, cuda_devices, period_s=0.004):
+        self.devs = list(cuda_devices)
+        self.period = period_s
+        self.rows = []  # (t, dev, sm_mhz, max_mhz, power_w, reason_bits)
+        self.marks = {}
+        self._stop = threading.Event()
+        self.t = None
+        self.error = None
 
     def __enter__(self):
         try:
-            self.proc = subprocess.Popen(["nvidia-smi", "--query-gpu=" + self.Q, "--format=csv,noheader,nounits",
-                                          "-lms", "100"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL,
-                                         text=True)
-            self.t = threading.Thread(target=self._read, daemon=True)
+            import pynvml
+            import torch
+
+            pynvml.nvmlInit()
+            self.nv = pynvml
+            self.handles = []
+            for d in self.devs:
+                try:
+                    uuid = str(torch.cuda.get_device_properties(d).uuid)
+                    h = pynvml.nvmlDeviceGetHandleByUUID(uuid if uuid.startswith("GPU-") else "GPU-" + uuid)
+                except Exception:  # noqa: BLE001
+                    h = pynvml.nvmlDeviceGetHandleByIndex(d)
+                self.handles.append((d, h, pynvml.nvmlDeviceGetMaxClockInfo(h, pynvml.NVML_CLOCK_SM)))
+            get_reasons = getattr(pynvml, "nvmlDeviceGetCurrentClocksEventReasons", None) or \
+                pynvml.nvmlDeviceGetCurrentClocksThrottleReasons
+            self._reasons = get_reasons
+            self.t = threading.Thread(target=self._run, daemon=True)
             self.t.start()
-        except Exception:
-            self.proc = None
+        except Exception as e:  # noqa: BLE001
+            self.error = f"{type(e).__name__}: {e}"[:200]
         return self
 
-    def _read(self):
-        for line in self.proc.stdout:
-            f = [s.strip() for s in line.split(",")]
-            if len(f) == 9:
-                self.rows.append(f)
+    def _run(self):
+        nv = self.nv
+        while not self._stop.is_set():
+            now = time.perf_counter()
+            for d, h, mx in self.handles:
+                try:
+                    sm = nv.nvmlDeviceGetClockInfo(h, nv.NVML_CLOCK_SM)
+                    pw = nv.nvmlDeviceGetPowerUsage(h) / 1000.0
+                    rs = int(self._reasons(h))
+                    self.rows.append((now, d, sm, mx, pw, rs))
+                except Exception:  # noqa: BLE001
+                    pass
+            self._stop.wait(self.period)
+
+    def mark(self, name):
+        self.marks[name] = time.perf_counter()
 
     def __exit__(self, *a):
-        if self.proc:
-            self.proc.terminate()
-            try:
-                self.proc.wait(timeout=5)
-            except Exception:
-                self.proc.kill()
+        self._stop.set()
+        if self.t:
+            self.t.join(timeout=2)
 
-    def summary(self):
-        rows = [r for r in self.rows if r[0].isdigit() and int(r[0]) in self.gpus]
+    def summary(self, begin="timed_begin", end="timed_end"):
+        """Samples inside [begin, end]; when the region is shorter than the
+        polling period and holds none, the samples of the whole loaded
+        window (warm-up start to region end) stand in, and say so."""
+        if self.error and not self.rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [], "samples": 0, "error": self.error}
+        t0, t1 = self.marks.get(begin), self.marks.get(end)
+        rows = [r for r in self.rows if t0 is not None and t1 is not None and t0 <= r[0] <= t1]
+        scope = "timed region"
         if not rows:
-            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [], "samples": 0}
-        sm = [float(r[1]) for r in rows if r[1].replace(".", "").isdigit()]
-        mx = [float(r[2]) for r in rows if r[2].replace(".", "").isdigit()]
-        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        reasons = sorted({names[i] for r in rows for i in range(4) if r[5 + i].lower() == "active"})
-        pw = [float(r[3]) for r in rows if re.match(r"^[0-9.]+$", r[3])]
-        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(mx) if mx else None,
-                "reasons": reasons, "samples": len(rows), "power_w_max": max(pw) if pw else None}
+            w0 = self.marks.get("window_begin", t0)
+            rows = [r for r in self.rows if w0 is not None and t1 is not None and w0 <= r[0] <= t1]
+            scope = "warm-up + timed region (region shorter than the polling period)"
+        if not rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [], "samples": 0, "scope": scope}
+        reasons = sorted({name for r in rows for bit, name in self.REASONS.items() if r[5] & bit})
+        return {"sm_mhz": statistics.median(r[2] for r in rows), "sm_max_mhz": max(r[3] for r in rows),
+                "sm_mhz_min": min(r[2] for r in rows), "reasons": reasons, "samples": len(rows),
+                "power_w_max": max(r[4] for r in rows), "scope": scope, "source": "NVML, polled every "
+                f"{self.period * 1e3:.0f} ms"}
 
 
 def cpu_port_run(x, wg, wu, rows, threads):
@@ -189,7 +245,10 @@ def reference_arm(args):
     sample = (f"each step: {rows} of {M} token rows x full N={N}, K={K} (bounded sample of the workload); "
               f"CPU restatement of the reference's fused AVX2 schedule (oracle/swiglu_port.c) on {threads} threads")
     line = {"impl": "reference", "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world,
-            "steps": args.steps, "warmup": args.warmup, "ms_per_step": mean * 1e3 * M / rows,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": mean * 1e3, "sample_rows": rows,
+            "ms_per_step_what": f"measured time of one step as run: {rows} token rows x full N, K (the rate "
+                                f"`value` is 4*rows*N*K / that time); the whole {M}-row workload would take "
+                                f"about {mean * 1e3 * M / rows:.0f} ms per step at this rate",
             "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
             "data": "synthetic (seeded splitmix64/Box-Muller, X~N(0,1), W~N(0,0.02), bf16)",
             "config": {"workload": "c3 llama7b-prefill swiglu", "M": M, "K": K, "N": N, "sample_rows": rows},
@@ -266,6 +325,61 @@ def time_steps(fn, flush, steps, stream):
     return [s.elapsed_time(e) for s, e in evs]
 
 
+def _bits(t):
+    """bf16 torch tensor (any device) -> numpy uint16 bit patterns."""
+    import torch
+
+    return t.detach().contiguous().cpu().view(torch.int16).numpy().view(np.uint16)
+
+
+def points_rel_err(x, wg, wu, y, rows, cols):
+    """max |y - ref| / max |ref| over the points (rows[i], cols[i]) of y,
+    ref = the FP64 oracle (oracle/swiglu_oracle.c, the checker) on the same
+    bf16 inputs.  x [M, K], wg / wu [K, n] (numpy uint16 bit patterns or
+    bf16 torch tensors on any device), y [M, n] torch (bf16 or f32).  Only
+    the rows of X and columns of W the points touch are copied to the host."""
+    import torch
+
+    import oracle
+
+    rows = np.asarray(rows, np.int64)
+    cols = np.asarray(cols, np.int64)
+    ur, ri = np.unique(rows, return_inverse=True)
+    uc, ci = np.unique(cols, return_inverse=True)
+
+    def take(t, idx, dim):
+        if isinstance(t, np.ndarray):
+            return np.ascontiguousarray(np.take(t, idx, axis=dim))
+        return _bits(t.index_select(dim, torch.as_tensor(idx, device=t.device)))
+
+    xc, gc, uc_ = take(x, ur, 0), take(wg, uc, 1), take(wu, uc, 1)
+    ref = oracle.swiglu_fp64_points(xc, gc, uc_, ri, ci)
+    yv = y[torch.as_tensor(rows, device=y.device), torch.as_tensor(cols, device=y.device)]
+    yv = yv.double().cpu().numpy()
+    if not np.all(np.isfinite(yv)):
+        return float("inf")
+    return float(np.abs(yv - ref).max() / max(np.abs(ref).max(), 1e-30))
+
+
+def parity_points(M, n, seed, boundaries=(), n_random=2048):
+    """Check points of an [M, n] output: n_random seeded random points, one
+    whole row, and the two columns on either side of every boundary (shard
+    edges) at 64 rows."""
+    rng = np.random.default_rng(seed)
+    rows = [rng.integers(0, M, n_random), np.full(n, int(rng.integers(0, M)))]
+    cols = [rng.integers(0, n, n_random), np.arange(n)]
+    for b in boundaries:
+        for c in (b - 1, b):
+            if 0 <= c < n:
+                r = rng.integers(0, M, 64)
+                rows.append(r)
+                cols.append(np.full(64, c))
+    return np.concatenate(rows), np.concatenate(cols)
+
+
+TOL_BF16 = 1e-2  # bf16 Y: max |y - ref| <= 1e-2 * max |ref| (the north star's tolerance)
+
+
 def our_arm(args):
     import torch
     import torch.distributed as dist
@@ -305,33 +419,37 @@ def our_arm(args):
         if world > 1:
             dist.barrier(device_ids=[local])
 
-    def max_over_ranks(v):
+    def reduce_over_ranks(v, op):
         if world == 1:
             return v
         t = torch.tensor([v], dtype=torch.float64, device=dev)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        dist.all_reduce(t, op=op)
         return float(t.item())
+
+    def max_over_ranks(v):
+        return reduce_over_ranks(v, dist.ReduceOp.MAX if world > 1 else None)
 
     def sum_over_ranks(v):
-        if world == 1:
-            return v
-        t = torch.tensor([v], dtype=torch.float64, device=dev)
-        dist.all_reduce(t, op=dist.ReduceOp.SUM)
-        return float(t.item())
+        return reduce_over_ranks(v, dist.ReduceOp.SUM if world > 1 else None)
 
     # ---------------------------------------------------------- value
+    sampler = ClockSampler(range(world)) if local == 0 else None
+    if sampler:
+        sampler.__enter__()
+        sampler.mark("window_begin")
     for i in range(args.warmup):
         step(i)
     torch.cuda.synchronize()
     llk.synchronize(local)
     barrier()
     torch.cuda.synchronize()
-    sampler = ClockSampler(range(world)) if local == 0 else None
     if sampler:
-        sampler.__enter__()
+        sampler.mark("timed_begin")
     t_wall0 = time.perf_counter()
     kernel_ms = time_back_to_back(step, args.steps, stream)
     t_wall = time.perf_counter() - t_wall0
+    if sampler:
+        sampler.mark("timed_end")
     barrier()
     torch.cuda.synchronize()
     if sampler:
@@ -340,12 +458,21 @@ def our_arm(args):
     job_ms = max_over_ranks(kernel_ms) / args.steps
     total_flops = 4.0 * M * N * K
     value = total_flops / (job_ms * 1e-3) / 1e12
+    clocks = sampler.summary() if sampler else None
+
+    # ------------------------------------------------------- parity (this rank's shard)
+    parity = {}
+    rows, cols = parity_points(M, n_r, seed=1000 + rank)
+    err = points_rel_err(x, wg_s, wu_s, sets[0][3], rows, cols)
+    parity["headline_shard"] = {"max_rel_err": max_over_ranks(err), "points_per_rank": int(rows.size)}
 
     # ------------------------------------------------------- roofline
-    peak_tf, peak_gbs, peak_src = measured_peaks()
+    peaks = measured_peaks()
+    peak_tf, peak_kind, peak_why = choose_peak(peaks, kernel_ms * 1e-3, clocks)
     my_ms = kernel_ms / args.steps
     achieved = 4.0 * M * n_r * K / (my_ms * 1e-3) / 1e12
-    traffic = profile_traffic("tc2_swiglu_c3") if world == 1 else None
+    traffic = profile_traffic("tc2_swiglu_c3", n_r)
+    alg_bytes = 2 * M * K + 4 * K * n_r + 2 * M * n_r
 
     # ----------------------------------------------------------- e2e
     # Through the reference-facing C ABI (llk_swiglu) with pinned host
@@ -372,6 +499,7 @@ def our_arm(args):
     e2e = {"value": total_flops / (e2e_ms * 1e-3) / 1e12, "unit": UNIT, "h2d_bytes_per_step": int(h2d),
            "d2h_bytes_per_step": int(d2h), "ms_per_step": e2e_ms,
            "path": "llk_swiglu C ABI, pinned host X/Wg/Wu/Y, copies in the timed region"}
+    parity["e2e_host_buffers"] = {"max_rel_err": max_over_ranks(points_rel_err(x, wg_s, wu_s, yh, rows, cols))}
     # Packed weights (PackedWeights + L4-cache role): weights resident,
     # X in / Y out per step.
     pw = llk.PackedWeights(gd, ud)
@@ -391,18 +519,20 @@ def our_arm(args):
     extras = {}
     n_sets = len(sets)
     if world > 1:
-        extras["gather_y"] = secondary(lambda: gather_timing(args, dev, stream, yd, N, world, barrier, max_over_ranks))
+        extras["gather_y"] = secondary(lambda: gather_timing(args, dev, stream, yd, N, world, barrier, max_over_ranks,
+                                                             (x, wg, wu)))
         if "error" not in extras["gather_y"]:
             extras["fused_allgather"] = secondary(lambda: fused_allgather_timing(
-                args, dev, stream, xd, gd, ud, N, barrier, max_over_ranks, job_ms, extras["gather_y"]["ms"]))
+                args, dev, stream, xd, gd, ud, N, barrier, max_over_ranks, job_ms, extras["gather_y"]["ms"],
+                (x, wg, wu)))
     cpu = None
     if not args.quick:
         del sets, xd, gd, ud, yd
         torch.cuda.empty_cache()
-        extras.update(secondary(lambda: sharded_extras(args, dev, stream, rank, world, peak_tf, peak_gbs, barrier,
+        extras.update(secondary(lambda: sharded_extras(args, dev, stream, rank, world, peaks, barrier,
                                                        max_over_ranks), "sharded_extras"))
         if world == 1:
-            extras.update(secondary(lambda: single_gpu_extras(args, dev, stream, peak_tf, peak_gbs),
+            extras.update(secondary(lambda: single_gpu_extras(args, dev, stream, peaks, value),
                                     "single_gpu_extras"))
             if not args.no_cpu_baseline:
                 cpu = cpu_baseline(x, wg, wu)
@@ -410,7 +540,30 @@ def our_arm(args):
                 if naive:
                     cpu["reference_naive"] = naive
 
-    clocks = sampler.summary() if sampler else None
+    # every parity figure of the run, headline and secondary, in one place
+    for key in ("gather_y", "fused_allgather"):
+        if isinstance(extras.get(key), dict) and "parity" in extras[key]:
+            parity[key] = extras[key]["parity"]
+    for key, sub in (("decode_c4", None), ("swiglu_c5", None)):
+        v = extras.get(key)
+        if isinstance(v, dict):
+            if "parity" in v:
+                parity[key] = v["parity"]
+            for cfg, r in v.items():
+                if isinstance(r, dict) and "parity" in r:
+                    parity[f"{key}.{cfg}"] = r["parity"]
+    expected = ["headline_shard", "e2e_host_buffers"]
+    if world > 1:
+        expected += ["gather_y", "fused_allgather"]
+    if not args.quick:
+        expected += ["decode_c4.c4_m1", "decode_c4.c4_m4", "decode_c4.c4_m16", "swiglu_c5"]
+    missing = [k for k in expected if k not in parity]
+    worst = max((p["max_rel_err"] for p in parity.values()), default=float("inf"))
+    parity_line = {"max_rel_err": worst, "tol": TOL_BF16, "ok": bool(worst <= TOL_BF16 and not missing),
+                   "missing": missing, "checks": parity,
+                   "oracle": "FP64 at sampled points (oracle/swiglu_oracle.c), every rank its own columns; full-Y "
+                             "paths: every rank the whole Y incl. both sides of each shard boundary"}
+
     if rank == 0:
         line = {
             "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
@@ -425,12 +578,18 @@ def our_arm(args):
                        "timing": "one CUDA event pair around all timed steps (launches back to back), "
                                  "max over ranks"},
             "roofline": {"bound": "tensor", "achieved": achieved, "peak": peak_tf, "unit": "TFLOP/s",
-                         "frac": achieved / peak_tf, "traffic": traffic,
-                         "peak_source": f"{peak_src} bf16 sustained (MEASURED_PEAKS.json bf16_tflops_sustained): "
-                                        "the timed loop is back to back and power-capped",
-                         "kernel": "tc2_kernel<TC_SWIGLU_BF16> (CTA pairs)" if M > 128 else "tc_swiglu_kernel<TC_SWIGLU_BF16>",
-                         "algorithmic_work": "4*M*N_rank*K FLOP per launch"},
+                         "frac": achieved / peak_tf, "peak_kind": peak_kind,
+                         "peak_why": f"{peaks['source']} bf16 {peak_kind}: {peak_why}",
+                         "frac_of_burst": achieved / peaks["burst"],
+                         "frac_of_sustained": achieved / peaks["sustained"],
+                         "traffic": traffic["bytes"] if traffic else None,
+                         "traffic_source": traffic["source"] if traffic else "no ncu capture of this shard width",
+                         "algorithmic_bytes": alg_bytes,
+                         "kernel": "tc2_kernel<TC_SWIGLU_BF16> (CTA pairs)" if M > 128 else
+                                   "tc_swiglu_kernel<TC_SWIGLU_BF16>",
+                         "algorithmic_work": "4*M*N_rank*K FLOP per launch (rank 0's shard)"},
             "e2e": e2e, "e2e_packed_weights": e2e_packed,
+            "parity": parity_line,
             "gpu_launches": args.steps,
             "clocks": clocks,
             "wall_s_timed_region": t_wall,
@@ -442,10 +601,23 @@ def our_arm(args):
     if world > 1:
         dist.barrier(device_ids=[local])
         dist.destroy_process_group()
+    if not parity_line["ok"]:
+        print(f"PARITY FAILURE: max rel err {worst:.3e} > {TOL_BF16}: {json.dumps(parity)}", file=sys.stderr)
+        return 3
     return 0
 
 
-def gather_timing(args, dev, stream, yd, N, world, barrier, max_over_ranks):
+def full_y_parity(y_full, host_inputs, bounds, rank, max_over_ranks):
+    """Every rank checks the whole Y it holds: random points, one whole row
+    and both sides of every shard boundary, against the FP64 oracle."""
+    x, wg, wu = host_inputs
+    M, N = y_full.shape
+    rows, cols = parity_points(M, N, seed=2000 + rank, boundaries=[b for b, _ in bounds[1:]])
+    err = points_rel_err(x, wg, wu, y_full, rows, cols)
+    return {"max_rel_err": max_over_ranks(err), "points_per_rank": int(rows.size)}
+
+
+def gather_timing(args, dev, stream, yd, N, world, barrier, max_over_ranks, host_inputs):
     """Optional full-Y path: NCCL all-gather of the padded shards plus the
     llk_gather_columns relayout -- timed apart from the kernel."""
     import torch
@@ -473,8 +645,12 @@ def gather_timing(args, dev, stream, yd, N, world, barrier, max_over_ranks):
     t = time_steps(step, None, steps, stream)
     ms = max_over_ranks(sum(t)) / steps
     recv = (world - 1) * M * width * yd.element_size()
+    torch.cuda.synchronize()
+    rank = dist.get_rank()
+    par = full_y_parity(y_full, host_inputs, bounds, rank, max_over_ranks)
     return {"ms": ms, "bytes_received_per_gpu": recv, "GB/s_per_gpu": recv / (ms * 1e-3) / 1e9,
-            "what": "all_gather_into_tensor (NCCL) of padded Y shards + llk_gather_columns relayout"}
+            "what": "all_gather_into_tensor (NCCL) of padded Y shards + llk_gather_columns relayout",
+            "parity": par}
 
 
 def secondary(fn, key=None):
@@ -492,7 +668,8 @@ def secondary(fn, key=None):
         return {key: err} if key else err
 
 
-def fused_allgather_timing(args, dev, stream, xd, gd, ud, N, barrier, max_over_ranks, kernel_ms, gather_ms):
+def fused_allgather_timing(args, dev, stream, xd, gd, ud, N, barrier, max_over_ranks, kernel_ms, gather_ms,
+                           host_inputs):
     """The full-Y path with the all-gather fused into the kernel
     (llk_swiglu_column_parallel: each rank's epilogue stores its columns
     into every rank's Y over NVLink, plus the entry / exit barriers), against
@@ -511,17 +688,30 @@ def fused_allgather_timing(args, dev, stream, xd, gd, ud, N, barrier, max_over_r
     ms = max_over_ranks(time_back_to_back(lambda i: layer(xd), steps, stream)) / steps
     torch.cuda.synchronize()
     barrier()
+    # The Y of the last timed call, as this rank holds it (its own columns
+    # written locally, every other rank's columns stored by that rank's kernel
+    # over NVLink).
+    y_last = layer.y(M).clone()
+    torch.cuda.synchronize()
+    barrier()
     layer.close()
+    from dslcompiler_b200.sharding import shard_bounds
+
+    par = full_y_parity(y_last, host_inputs, shard_bounds(N, layer.world), layer.rank, max_over_ranks)
     flops = 4.0 * M * N * K
-    return {"ms": ms, "tflops_whole_job": flops / (ms * 1e-3) / 1e12,
+    bytes_out = (layer.world - 1) * M * (layer.end - layer.begin) * 2
+    return {"ms": ms, "tflops_whole_job": flops / (ms * 1e-3) / 1e12, "parity": par,
+            "nvlink_bytes_out_per_gpu": bytes_out, "GB/s_out_per_gpu": bytes_out / (ms * 1e-3) / 1e9,
             "kernel_plus_nccl_gather_ms": kernel_ms + gather_ms,
             "tflops_kernel_plus_nccl_gather": flops / ((kernel_ms + gather_ms) * 1e-3) / 1e12,
             "what": "llk_swiglu_column_parallel: full Y on every GPU, shards stored to peers by the kernel epilogue"}
 
 
-def single_gpu_extras(args, dev, stream, peak_tf, peak_gbs):
-    """Secondary measurement on one GPU: the micro.mma matmul (config 2),
-    same timing rules."""
+def single_gpu_extras(args, dev, stream, peaks, headline_tflops):
+    """Secondary measurements on one GPU, same timing rules: the micro.mma
+    matmul (config 2), and a cuBLAS yardstick (torch.matmul, a library GEMM
+    timed beside ours, not part of the product) for both config 3 -- the
+    same FLOPs as X.[Wg|Wu] with no epilogue -- and config 2."""
     import torch
 
     import dslcompiler_b200 as llk
@@ -542,11 +732,56 @@ def single_gpu_extras(args, dev, stream, peak_tf, peak_gbs):
     for i in range(3):
         fn(i)
     ms = time_back_to_back(fn, steps, stream) / steps
-    out["matmul_c2"] = {"tflops": 2.0 * 4096 ** 3 / (ms * 1e-3) / 1e12, "ms": ms,
-                        "frac_of_peak": 2.0 * 4096 ** 3 / (ms * 1e-3) / 1e12 / peak_tf}
-    del ad, bd, cd, msets
     torch.cuda.synchronize()
     llk.synchronize(dev.index)
+    mm_tf = 2.0 * 4096 ** 3 / (ms * 1e-3) / 1e12
+    # parity: 2048 points of C against an f64 dot product of the bf16 operands
+    rng = np.random.default_rng(7)
+    r, c = rng.integers(0, 4096, 2048), rng.integers(0, 4096, 2048)
+    af = torch.from_numpy(a.view(np.int16)).view(torch.bfloat16).double()
+    bf = torch.from_numpy(b.view(np.int16)).view(torch.bfloat16).double()
+    ref = (af[torch.as_tensor(r)] * bf[:, torch.as_tensor(c)].T).sum(1).numpy()
+    got = msets[0][2][torch.as_tensor(r, device=dev), torch.as_tensor(c, device=dev)].double().cpu().numpy()
+    mm_err = float(np.abs(got - ref).max() / np.abs(ref).max())
+
+    # cuBLAS on the same shapes and rotation
+    def cublas_ms(A, B, out_dtype):
+        sets_, _ = input_sets(dev, [A, B], l2)
+        kw = {"out_dtype": out_dtype} if out_dtype is not None else {}
+
+        def g(i):
+            x_, w_ = sets_[i % len(sets_)]
+            torch.mm(x_, w_, **kw)
+
+        for i in range(3):
+            g(i)
+        return time_back_to_back(g, steps, stream) / steps
+
+    try:
+        cb2_ms = cublas_ms(ad, bd, torch.float32)
+        cb2_what = "torch.mm bf16 x bf16 -> f32 (out_dtype)"
+    except (TypeError, RuntimeError):
+        cb2_ms = cublas_ms(ad, bd, None)
+        cb2_what = "torch.mm bf16 x bf16 -> bf16"
+    cb2_tf = 2.0 * 4096 ** 3 / (cb2_ms * 1e-3) / 1e12
+    out["matmul_c2"] = {"tflops": mm_tf, "ms": ms, "frac_of_burst": mm_tf / peaks["burst"],
+                        "frac_of_sustained": mm_tf / peaks["sustained"], "parity": {"max_rel_err": mm_err},
+                        "cublas_tflops": cb2_tf, "vs_cublas": mm_tf / cb2_tf, "cublas_what": cb2_what}
+    del ad, bd, cd, msets
+    torch.cuda.empty_cache()
+
+    c = CONFIG
+    g = torch.Generator(device=dev).manual_seed(3)
+    X = (torch.randn((c["M"], c["K"]), generator=g, device=dev) * c["x_std"]).bfloat16()
+    W = (torch.randn((c["K"], 2 * c["N"]), generator=g, device=dev) * c["w_std"]).bfloat16()
+    cb3_ms = cublas_ms(X, W, None)
+    cb3_tf = 4.0 * c["M"] * c["N"] * c["K"] / (cb3_ms * 1e-3) / 1e12
+    out["cublas_c3"] = {"tflops": cb3_tf, "ms": cb3_ms, "ours_tflops": headline_tflops,
+                        "vs_cublas": headline_tflops / cb3_tf,
+                        "what": "torch.mm X[2048,4096] x [Wg|Wu][4096,22016] bf16 -> bf16 (same FLOPs, no SiLU "
+                                "epilogue), same rotation and timing as the headline, measured right after it"}
+    del X, W
+    torch.cuda.empty_cache()
     return out
 
 
@@ -561,12 +796,13 @@ def device_normal_bf16(shape, std, seed, dev):
     return (torch.randn(shape, generator=g, device=dev, dtype=torch.float32) * std).to(torch.bfloat16)
 
 
-def sharded_extras(args, dev, stream, rank, world, peak_tf, peak_gbs, barrier, max_over_ranks):
+def sharded_extras(args, dev, stream, rank, world, peaks, barrier, max_over_ranks):
     """Secondary configurations at every GPU count, column-sharded like the
     headline (rank r computes its llk_shard_columns share, no collective):
     config 5 (Llama-70B prefill SwiGLU, 7.7 TFLOP) and the config-4 decode
     shapes.  Whole-job figures from the max over ranks of back-to-back
-    CUDA-event time, inputs rotating over sets larger than 2x L2."""
+    CUDA-event time, inputs rotating over sets larger than 2x L2.  Every
+    rank checks its shard against the FP64 oracle at sampled points."""
     import torch
 
     import dslcompiler_b200 as llk
@@ -594,27 +830,74 @@ def sharded_extras(args, dev, stream, rank, world, peak_tf, peak_gbs, barrier, m
         torch.cuda.synchronize()
         barrier()
         ms = max_over_ranks(time_back_to_back(fn, steps, stream)) / steps
+        torch.cuda.synchronize()
         llk.synchronize(dev.index)
+        rows, cols = parity_points(M, e - b, seed=seed + 17 * rank, n_random=1024)
+        err = max_over_ranks(points_rel_err(xd, gd, ud, sets[0][3], rows, cols))
         del sets, xd, gd, ud, yd
         torch.cuda.empty_cache()
-        return M, K, N, ms
+        return M, K, N, e - b, ms, {"max_rel_err": err, "points_per_rank": int(rows.size)}
 
     dec = {}
     for i, cfg in enumerate(("c4_m1", "c4_m4", "c4_m16")):
-        M, K, N, ms = run(cfg, max(5, min(args.steps, 200)), 41 + i)
+        M, K, N, n_r, ms, par = run(cfg, max(5, min(args.steps, 200)), 41 + i)
         byts = 2 * M * K + 4 * K * N + 2 * M * N
         dec[cfg] = {"us": ms * 1e3, "GB/s": byts / (ms * 1e-3) / 1e9,
-                    "frac_of_hbm_per_gpu": byts / (ms * 1e-3) / 1e9 / world / peak_gbs,
-                    "tflops": 4.0 * M * N * K / (ms * 1e-3) / 1e12}
+                    "frac_of_hbm_per_gpu": byts / (ms * 1e-3) / 1e9 / world / peaks["hbm"],
+                    "shard_cols_rank0": n_r, "tflops": 4.0 * M * N * K / (ms * 1e-3) / 1e12, "parity": par}
     out["decode_c4"] = dec
     # config 5 after the decode shapes: its seconds at the power cap lower the
     # SM clock for a few seconds afterwards, which slows the decode kernel.
-    M, K, N, ms = run("c5", max(5, min(args.steps, 40)), 55)
+    M, K, N, n_r, ms, par = run("c5", max(5, min(args.steps, 40)), 55)
     tf = 4.0 * M * N * K / (ms * 1e-3) / 1e12
     out["swiglu_c5"] = {"workload": "c5 llama70b-prefill swiglu X[8192,8192] W[8192,28672] bf16",
-                        "tflops": tf, "ms": ms, "frac_of_peak_per_gpu": tf / world / peak_tf,
+                        "tflops": tf, "ms": ms, "frac_of_sustained_per_gpu": tf / world / peaks["sustained"],
+                        "frac_of_burst_per_gpu": tf / world / peaks["burst"], "shard_cols_rank0": n_r,
+                        "parity": par,
                         "data": "synthetic, drawn on the device (torch Philox, seeded), X~N(0,1), W~N(0,0.015)"}
     return out
+
+
+def profile_case(args):
+    """Runs one configuration's kernel a few times on cuda:0 with per-launch
+    CUDA-event times, for ncu captures and quick timing.  Inputs are seeded
+    random tensors of the configuration's shapes, drawn on the device;
+    --shape M,K,N runs a SwiGLU of that shape instead (e.g. a column shard)."""
+    import torch
+
+    import dslcompiler_b200 as llk
+    from dslcompiler_b200 import datagen as dg
+
+    if args.profile_case == "shape":
+        M_, K_, N_ = (int(v) for v in args.shape.split(","))
+        c = dict(kind="swiglu", M=M_, K=K_, N=N_, x_std=1.0, w_std=0.02, y="bf16")
+    else:
+        c = dg.CONFIGS[args.profile_case]
+    g = torch.Generator(device="cuda").manual_seed(42)
+    M, K, N = c["M"], c["K"], c["N"]
+    if c["kind"] == "matmul":
+        A = (torch.rand((M, K), generator=g, device="cuda") * 2 - 1).bfloat16()
+        B = (torch.rand((K, N), generator=g, device="cuda") * 2 - 1).bfloat16()
+        C = torch.empty((M, N), dtype=torch.float32, device="cuda")
+        run = lambda: llk.matmul(A, B, C, variant=args.variant)  # noqa: E731
+    else:
+        X = (torch.randn((M, K), generator=g, device="cuda") * c["x_std"]).bfloat16()
+        Wg = (torch.randn((K, N), generator=g, device="cuda") * c["w_std"]).bfloat16()
+        Wu = (torch.randn((K, N), generator=g, device="cuda") * c["w_std"]).bfloat16()
+        Y = torch.empty((M, N), dtype=torch.float32 if c["y"] == "f32" else torch.bfloat16, device="cuda")
+        run = lambda: llk.fused_swiglu(X, Wg, Wu, out=Y, out_dtype=c["y"], variant=args.variant)  # noqa: E731
+    s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    times = []
+    for _ in range(args.launches):
+        s.record()
+        run()
+        e.record()
+        torch.cuda.synchronize()
+        times.append(s.elapsed_time(e))
+    llk.synchronize(0)
+    print(f"{args.profile_case} M={M} K={K} N={N}: {args.launches} launches, ms per launch "
+          f"{[round(t, 4) for t in times]}", file=sys.stderr)
+    return 0
 
 
 def main(argv=None):
@@ -625,7 +908,15 @@ def main(argv=None):
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--quick", action="store_true", help="skip the single-GPU extras and the CPU baseline")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--profile-case", default=None, metavar="CFG",
+                    help="run one configuration's kernel --launches times on cuda:0 (for ncu) and exit; CFG is a "
+                         "config name (c1 .. c5, c4_m1 ..) or 'shape' with --shape M,K,N")
+    ap.add_argument("--shape", default=None)
+    ap.add_argument("--launches", type=int, default=3)
+    ap.add_argument("--variant", default="auto")
     args = ap.parse_args(argv)
+    if args.profile_case:
+        return profile_case(args)
     if args.warmup < 3:
         args.warmup = 3
     rank, _, world = dist_env()

@@ -27,6 +27,10 @@ LLK_ERR_NOMEM = 9
 LLK_ERR_NOT_FOUND = 10
 LLK_IPC_HANDLE_BYTES = 64
 
+# include/llk_b200.h: the no-allocation decode entry point's limits
+LLK_DECODE_NOALLOC_SCRATCH_BYTES = 16 << 20
+LLK_DECODE_NOALLOC_MAX_N = 65536 * 128
+
 # enum llk_dtype (KernelKey.h DType)
 LLK_DTYPE_BF16 = 0
 LLK_DTYPE_FP16 = 1

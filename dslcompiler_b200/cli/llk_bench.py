@@ -6,8 +6,8 @@ warmup-ms, then `reps` windows of measure-ms, report the best GFLOPS with the
 op's FLOP count) and the same two output lines.  Unlike the reference, which
 times a stand-in loop (llk-bench.cpp:37-53), this times the real fused SwiGLU
 (4MNK FLOP) or matmul (2MNK) kernel on the GPU; each window is timed with CUDA
-events.  --cpu times the CPU restatement of the reference's fused schedule on
---threads host threads instead (oracle/, a baseline, not the product).
+events.  (The CPU baseline with the same flags and output lines is
+``python -m oracle.cpu_bench``, test infrastructure outside this package.)
 """
 from __future__ import annotations
 
@@ -47,54 +47,34 @@ def main(argv=None) -> int:
     ap.add_argument("--variant", choices=["auto", "tc", "decode", "simt"], default="auto")
     ap.add_argument("--device", type=int, default=0)
     ap.add_argument("--packed", action="store_true", help="use packed (slab-major) weights")
-    ap.add_argument("--cpu", action="store_true", help="time the CPU restatement instead (baseline)")
     ap.add_argument("--json", action="store_true")
     a = ap.parse_args(argv)
     M, N, K = a.M, a.N, a.K
     flop = (4.0 if a.op == "swiglu" else 2.0) * M * N * K
     print(f"LLK Bench — M={M} N={N} K={K} threads={a.threads}")
 
-    if a.cpu:
-        import numpy as np  # noqa: F401
+    import torch
 
-        import oracle
-        from dslcompiler_b200 import datagen as dg
+    import dslcompiler_b200 as llk
 
-        x, wg, wu = dg.swiglu_inputs(M, K, N, 1.0, 0.02, seed=1)
-        fn = (lambda: oracle.port_swiglu(x, wg, wu, "bf16", threads=a.threads)) if a.op == "swiglu" else \
-            (lambda: oracle.port_matmul(x, wg, threads=a.threads))
-
-        def window(budget):
-            t0, it = time.perf_counter(), 0
-            while True:
-                fn()
-                it += 1
-                el = (time.perf_counter() - t0) * 1e3
-                if el >= budget:
-                    return el, it
-    else:
-        import torch
-
-        import dslcompiler_b200 as llk
-
-        torch.cuda.set_device(a.device)
-        g = torch.Generator(device="cuda").manual_seed(1)
-        X = torch.randn((M, K), generator=g, device="cuda").bfloat16()
-        Wg = (torch.randn((K, N), generator=g, device="cuda") * 0.02).bfloat16()
-        if a.op == "swiglu":
-            Wu = (torch.randn((K, N), generator=g, device="cuda") * 0.02).bfloat16()
-            Y = torch.empty((M, N), dtype=torch.bfloat16, device="cuda")
-            if a.packed:
-                pw = llk.PackedWeights(Wg, Wu)
-                fn = lambda: pw(X, out=Y, variant=a.variant)  # noqa: E731
-            else:
-                fn = lambda: llk.fused_swiglu(X, Wg, Wu, out=Y, variant=a.variant)  # noqa: E731
+    torch.cuda.set_device(a.device)
+    g = torch.Generator(device="cuda").manual_seed(1)
+    X = torch.randn((M, K), generator=g, device="cuda").bfloat16()
+    Wg = (torch.randn((K, N), generator=g, device="cuda") * 0.02).bfloat16()
+    if a.op == "swiglu":
+        Wu = (torch.randn((K, N), generator=g, device="cuda") * 0.02).bfloat16()
+        Y = torch.empty((M, N), dtype=torch.bfloat16, device="cuda")
+        if a.packed:
+            pw = llk.PackedWeights(Wg, Wu)
+            fn = lambda: pw(X, out=Y, variant=a.variant)  # noqa: E731
         else:
-            C = torch.empty((M, N), dtype=torch.float32, device="cuda")
-            fn = lambda: llk.matmul(X, Wg, C, variant=a.variant)  # noqa: E731
+            fn = lambda: llk.fused_swiglu(X, Wg, Wu, out=Y, variant=a.variant)  # noqa: E731
+    else:
+        C = torch.empty((M, N), dtype=torch.float32, device="cuda")
+        fn = lambda: llk.matmul(X, Wg, C, variant=a.variant)  # noqa: E731
 
-        def window(budget):
-            return gpu_window(fn, budget)
+    def window(budget):
+        return gpu_window(fn, budget)
 
     window(a.warmup_ms)
     best_gflops, best_ms = 0.0, 0.0
@@ -104,14 +84,11 @@ def main(argv=None) -> int:
         gf = flop / (ms * 1e-3) / 1e9
         if gf > best_gflops:
             best_gflops, best_ms = gf, ms
-    if not a.cpu:
-        import dslcompiler_b200 as llk
-
-        llk.synchronize(a.device)
+    llk.synchronize(a.device)
     print(f"Best: {best_gflops} GFLOPS ({best_ms} ms/iter, {a.reps} reps)")
     if a.json:
         print(json.dumps({"M": M, "N": N, "K": K, "op": a.op, "gflops": best_gflops, "ms": best_ms,
-                          "device": "cpu" if a.cpu else "b200", "threads": a.threads if a.cpu else None}))
+                          "device": "b200"}))
     return 0
 
 

@@ -18,8 +18,12 @@ int decode_max_m();
 // Whether the decode kernel handles this shape / output type.
 bool decode_supported(int64_t M, int64_t N, int64_t K, int y_f32);
 DecodePlan decode_plan(int64_t M, int64_t N, int64_t K, int sm_count);
-// Device workspace the launch needs (split-K partial sums + tile counters).
-size_t decode_workspace_bytes(int64_t M, int64_t N, int64_t K, int sm_count);
+// Device workspace a launch of `grid` CTAs needs: 256 bytes reserved for the
+// CTA-pair kernel's work counter, the per-tile arrival counters, and (when
+// some CTA's range starts inside a tile) two partial-sum slots per CTA.
+size_t decode_workspace_bytes(int64_t M, int64_t N, int64_t K, int grid);
+// Largest grid whose partial-sum slots fit in `workspace_bytes`.
+int decode_max_grid_for(int64_t M, size_t workspace_bytes);
 // Byte offset and size of the per-tile counters inside the workspace; they
 // must be zero before the first launch (each launch leaves them zero again).
 size_t decode_counter_offset(int64_t M, int64_t N);

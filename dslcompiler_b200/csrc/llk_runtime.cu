@@ -136,6 +136,19 @@ bool is_device_ptr(const void *p) {
   return a.type == cudaMemoryTypeDevice || a.type == cudaMemoryTypeManaged;
 }
 
+// Device memory of a GPU other than `dev` (managed memory is not): the
+// kernels on `dev` would fault on it unless peer access happens to be
+// enabled, so the entry points that launch on `dev` refuse it.
+bool on_other_device(const void *p, int dev) {
+  if (!p) return false;
+  cudaPointerAttributes a;
+  if (cudaPointerGetAttributes(&a, p) != cudaSuccess) {
+    cudaGetLastError();
+    return false;
+  }
+  return a.type == cudaMemoryTypeDevice && a.device != dev;
+}
+
 // 2-D bf16 tensor map: dims {inner, outer}, row pitch in bytes, box
 // {box_inner, box_outer}, 128-byte swizzle, zero fill out of bounds.
 int encode_tmap(CUtensorMap *m, const void *base, uint64_t inner, uint64_t outer, uint64_t pitch_bytes,
@@ -361,7 +374,10 @@ int launch_device(DeviceState &ds, int op, const DevTensor &x, const DevTensor &
   }
 
   if (variant == LLK_VARIANT_DECODE) {
-    const size_t need = decode_workspace_bytes(M, N, K, ds.sm_count);
+    DecodePlan d = {plan.block_m, plan.block_n, plan.block_k, plan.stages, plan.split_k, plan.grid, plan.threads,
+                     plan.smem_bytes};
+    if (!decode_plan_valid(M, N, K, d)) d = decode_plan(M, N, K, ds.sm_count);
+    const size_t need = decode_workspace_bytes(M, N, K, d.grid);
     void *ws = scratch;
     if (ws != nullptr) {
       // Caller scratch: its tile counters start from an unknown state.
@@ -374,9 +390,6 @@ int launch_device(DeviceState &ds, int op, const DevTensor &x, const DevTensor &
       if (ds.workspace.ensure(need, true) != cudaSuccess) return LLK_ERR_NOMEM;
       ws = ds.workspace.ptr;
     }
-    DecodePlan d = {plan.block_m, plan.block_n, plan.block_k, plan.stages, plan.split_k, plan.grid, plan.threads,
-                     plan.smem_bytes};
-    if (!decode_plan_valid(M, N, K, d)) d = decode_plan(M, N, K, ds.sm_count);
     CUtensorMap tg, tu, tx;
     int rc;
     if ((rc = encode_weight_tmap(&tg, wg)) != LLK_OK) return rc;
@@ -673,6 +686,9 @@ int run_op(int op, const Tensor2D *x, const Tensor2D *wg, const Tensor2D *wu, Te
     const bool dx = is_device_ptr(x->data), dy = is_device_ptr(y->data);
     const bool dg = packed_g ? true : is_device_ptr(wg->data);
     const bool du = packed_g ? true : (wu == wg ? dg : is_device_ptr(wu->data));
+    if ((dx && on_other_device(x->data, dev)) || (dy && on_other_device(y->data, dev)) ||
+        (!packed_g && dg && on_other_device(wg->data, dev)) || (!packed_g && du && on_other_device(wu->data, dev)))
+      return LLK_ERR_ARG;
     std::lock_guard<std::mutex> lk(ds->mu);
     if (op == LLK_OP_FUSED_SWIGLU && !packed_g && x->data && wg->data && wu->data && y->data && !dx && !dg && !du &&
         !dy) {
@@ -1424,11 +1440,13 @@ int llk_swiglu_column_parallel(const Tensor2D *x, const Tensor2D *wg_shard, cons
   } else {
     if (wg_shard->dim0 != K || wg_shard->dim1 != w || wu_shard->dim0 != K || wu_shard->dim1 != w)
       return LLK_ERR_SHAPE;
-    if (!is_device_ptr(wg_shard->data) || !is_device_ptr(wu_shard->data)) return LLK_ERR_ARG;
+    if (!is_device_ptr(wg_shard->data) || !is_device_ptr(wu_shard->data) ||
+        on_other_device(wg_shard->data, g->device) || on_other_device(wu_shard->data, g->device))
+      return LLK_ERR_ARG;
     dg = dev_tensor(*wg_shard);
     du = dev_tensor(*wu_shard);
   }
-  if (M > 0 && !is_device_ptr(x->data)) return LLK_ERR_ARG;
+  if (M > 0 && (!is_device_ptr(x->data) || on_other_device(x->data, g->device))) return LLK_ERR_ARG;
   DeviceState *ds;
   int rc;
   if ((rc = device_init(g->device, &ds)) != LLK_OK) return rc;

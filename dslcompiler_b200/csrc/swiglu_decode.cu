@@ -13,10 +13,13 @@
 // per CTA, so every SM streams the same number of weight bytes whatever N/128
 // is.  A CTA's range covers one or more tile segments.  A tile owned by a
 // single CTA is finished straight from TMEM; a tile shared by several CTAs
-// has each contributor write its f32 partial sums to its own slot of the
-// workspace, and the last contributor to arrive (per-tile counter) adds the
-// slots in contributor order -- deterministic -- applies the SiLU * up
-// epilogue, stores Y and resets the counter to zero for the next launch.
+// has each contributor write its f32 partial sums (token rows < M only) to a
+// slot of its own, and the last contributor to arrive (per-tile counter)
+// adds the contributors' slots in CTA order -- deterministic -- applies the
+// SiLU * up epilogue, stores Y and resets the counter to zero for the next
+// launch.  Only a CTA's first and last tile can be shared, so the workspace
+// holds two slots per CTA and a tile may have any number of contributors:
+// a narrow column shard (a few tiles) still spreads over every SM.
 //
 // Roles: warp 0 TMA producer, warp 1 TMEM owner + MMA issuer, warps 2-5
 // epilogue (one TMEM lane = one output column each).  All waits bounded.
@@ -38,13 +41,16 @@ constexpr int kThreads = 192;
 constexpr int kTileN = 128;        // weight columns per tile (MMA M)
 constexpr int kBK = 64;            // k per stage
 constexpr uint32_t kSlab = 64 * kBK * 2;  // 64 n x 64 k bf16 = 8 KB
-constexpr int kMaxSlots = 4;       // contributors per tile the workspace holds
 constexpr uint64_t kWaitLimitNs = 2000000000ull;
 constexpr int kSmemBudget = 220 * 1024;
-// The per-tile counters sit at the start of the workspace, at the same place
-// for every shape, so a workspace reused across shapes never has a counter
-// landing on another call's partial sums.  256 KB = 65536 tiles (N <= 8 M).
+// Workspace layout, the same for every shape so a workspace reused across
+// shapes never has a counter landing on another call's partial sums:
+//   [0, 256)                 reserved for the CTA-pair kernel's work counter
+//   [256, 256 + 256 KB)      per-tile arrival counters (65536 tiles, N <= 8 M)
+//   [256 + 256 KB, ...)      partial sums, two slots per CTA.
+constexpr size_t kCounterOffset = 256;
 constexpr size_t kCounterRegion = 256 * 1024;
+constexpr size_t kPartialsOffset = kCounterOffset + kCounterRegion;
 
 struct DecodeParams {
   int M, N, K;
@@ -57,7 +63,7 @@ struct DecodeParams {
   int slab_major;    // weight tensor maps describe slab-major packed weights
   void *y;
   long long ldy;
-  float *partials;   // [n_tiles][kMaxSlots][2][Mp][128] f32
+  float *partials;   // [gridDim.x][2 slots][2 (gate, up)][Mp][128] f32
   int *counters;     // [n_tiles]
   int *status;
 };
@@ -245,10 +251,9 @@ __global__ void __launch_bounds__(kThreads, 1)
       const long long c_first = cta_of(t_begin, p.total, G);
       const long long c_last = cta_of(t_end - 1, p.total, G);
       const int n_contrib = static_cast<int>(c_last - c_first + 1);
-      const int slot = static_cast<int>(blockIdx.x - c_first);
       const int n = static_cast<int>(t) * kTileN + r;
       const uint32_t t_row = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + acc * acc_cols;
-      float *tile_ws = p.partials + (size_t)t * kMaxSlots * 2 * p.Mp * kTileN;
+      const size_t slot_floats = (size_t)2 * p.Mp * kTileN;
 
       if (n_contrib == 1) {
         for (int m0 = 0; m0 < p.Mp; m0 += 16) {
@@ -267,17 +272,20 @@ __global__ void __launch_bounds__(kThreads, 1)
         continue;
       }
 
-      // Shared tile: park this CTA's partial sums in its workspace slot.
-      float *mine = tile_ws + (size_t)slot * 2 * p.Mp * kTileN;
-      for (int m0 = 0; m0 < p.Mp; m0 += 16) {
+      // Shared tile: park this CTA's partial sums in its slot -- slot 0 when
+      // the tile is the one its range starts in, slot 1 for its last tile.
+      float *mine = p.partials + ((size_t)blockIdx.x * 2 + (t == w0 / p.kb_per_tile ? 0 : 1)) * slot_floats;
+      for (int m0 = 0; m0 < p.M; m0 += 16) {
         uint32_t g[16], uu[16];
         tmem_ld_32x32b_x16(t_row + m0, g);
         tmem_ld_32x32b_x16(t_row + p.Mp + m0, uu);
         tmem_ld_wait();
 #pragma unroll
         for (int j = 0; j < 16; ++j) {
-          mine[(size_t)(m0 + j) * kTileN + r] = __uint_as_float(g[j]);
-          mine[(size_t)(p.Mp + m0 + j) * kTileN + r] = __uint_as_float(uu[j]);
+          if (m0 + j < p.M) {
+            mine[(size_t)(m0 + j) * kTileN + r] = __uint_as_float(g[j]);
+            mine[(size_t)(p.Mp + m0 + j) * kTileN + r] = __uint_as_float(uu[j]);
+          }
         }
       }
       tc_fence_before();
@@ -295,24 +303,24 @@ __global__ void __launch_bounds__(kThreads, 1)
         // token rows at a time so the loads of a row block are in flight
         // together.
         for (int m0 = 0; m0 < p.M; m0 += 16) {
+          const int rows = p.M - m0 < 16 ? p.M - m0 : 16;
           float gs[16], us[16];
 #pragma unroll
           for (int j = 0; j < 16; ++j) gs[j] = us[j] = 0.f;
+          for (long long c = c_first; c <= c_last; ++c) {
+            // contributor c's slot for tile t (the same rule the writer used)
+            const int which = range_begin(c, p.total, G) / p.kb_per_tile == t ? 0 : 1;
+            const float *ps = p.partials + ((size_t)c * 2 + which) * slot_floats + (size_t)m0 * kTileN + r;
+            float gv[16], uv[16];
 #pragma unroll
-          for (int sl = 0; sl < kMaxSlots; ++sl) {
-            if (sl < n_contrib) {
-              const float *ps = tile_ws + (size_t)sl * 2 * p.Mp * kTileN + (size_t)m0 * kTileN + r;
-              float gv[16], uv[16];
+            for (int j = 0; j < 16; ++j) {
+              gv[j] = j < rows ? __ldcg(ps + (size_t)j * kTileN) : 0.f;
+              uv[j] = j < rows ? __ldcg(ps + (size_t)(p.Mp + j) * kTileN) : 0.f;
+            }
 #pragma unroll
-              for (int j = 0; j < 16; ++j) {
-                gv[j] = __ldcg(ps + (size_t)j * kTileN);
-                uv[j] = __ldcg(ps + (size_t)(p.Mp + j) * kTileN);
-              }
-#pragma unroll
-              for (int j = 0; j < 16; ++j) {
-                gs[j] += gv[j];
-                us[j] += uv[j];
-              }
+            for (int j = 0; j < 16; ++j) {
+              gs[j] += gv[j];
+              us[j] += uv[j];
             }
           }
           if (n < p.N) {
@@ -375,11 +383,8 @@ DecodePlan decode_plan(int64_t M, int64_t N, int64_t K, int sm_count) {
     grid = n_tiles;
     d.stages = d.stages < 4 ? d.stages : 4;
   }
-  // every CTA streams at least one k-block of each tile segment it touches,
-  // and no tile may be split over more CTAs than the workspace has slots
-  const long long kb_per_tile = (K + kBK - 1) / kBK;
-  const long long min_units = (kb_per_tile + kMaxSlots - 2) / (kMaxSlots - 1);
-  if (total / grid < min_units) grid = total / min_units;
+  // every CTA streams at least one work unit
+  if (grid > total) grid = total;
   if (grid < 1) grid = 1;
   d.grid = static_cast<int>(grid);
   d.split_k = static_cast<int>((grid + ((N + kTileN - 1) / kTileN) - 1) / ((N + kTileN - 1) / kTileN));
@@ -388,13 +393,24 @@ DecodePlan decode_plan(int64_t M, int64_t N, int64_t K, int sm_count) {
   return d;
 }
 
-size_t decode_workspace_bytes(int64_t M, int64_t N, int64_t, int) {
-  const int Mp = padded_m(M);
-  const size_t n_tiles = static_cast<size_t>((N + kTileN - 1) / kTileN);
-  return kCounterRegion + n_tiles * kMaxSlots * 2 * Mp * kTileN * sizeof(float);
+size_t decode_workspace_bytes(int64_t M, int64_t N, int64_t K, int grid) {
+  const long long kb_per_tile = (K + kBK - 1) / kBK;
+  const long long total = ((N + kTileN - 1) / kTileN) * kb_per_tile;
+  // Partial-sum slots only when some CTA range starts inside a tile.
+  bool shared = false;
+  for (long long c = 1; c < grid && !shared; ++c) shared = (c * total / grid) % kb_per_tile != 0;
+  if (!shared) return kPartialsOffset;
+  return kPartialsOffset + static_cast<size_t>(grid) * 2 * 2 * padded_m(M) * kTileN * sizeof(float);
 }
 
-size_t decode_counter_offset(int64_t, int64_t) { return 0; }
+int decode_max_grid_for(int64_t M, size_t workspace_bytes) {
+  if (workspace_bytes <= kPartialsOffset) return 0;
+  const size_t per_cta = static_cast<size_t>(2) * 2 * padded_m(M) * kTileN * sizeof(float);
+  const size_t g = (workspace_bytes - kPartialsOffset) / per_cta;
+  return g > INT32_MAX ? INT32_MAX : static_cast<int>(g);
+}
+
+size_t decode_counter_offset(int64_t, int64_t) { return kCounterOffset; }
 size_t decode_counter_bytes(int64_t N) { return static_cast<size_t>((N + kTileN - 1) / kTileN) * sizeof(int); }
 
 bool decode_plan_valid(int64_t M, int64_t N, int64_t K, const DecodePlan &d) {
@@ -404,10 +420,7 @@ bool decode_plan_valid(int64_t M, int64_t N, int64_t K, const DecodePlan &d) {
   if (d.stages * sb + static_cast<int>(sizeof(DecodeTail)) + 1024 > 227 * 1024) return false;
   const long long kb_per_tile = (K + kBK - 1) / kBK;
   const long long total = ((N + kTileN - 1) / kTileN) * kb_per_tile;
-  if (d.grid > total) return false;
-  // no tile may have more contributors than the workspace has slots
-  const long long min_units = (kb_per_tile + kMaxSlots - 2) / (kMaxSlots - 1);
-  return total / d.grid >= min_units;
+  return d.grid <= total;
 }
 
 cudaError_t decode_launch(const CUtensorMap &wg, const CUtensorMap &wu, const CUtensorMap &x, void *y, int64_t ldy,
@@ -427,8 +440,8 @@ cudaError_t decode_launch(const CUtensorMap &wg, const CUtensorMap &wu, const CU
   p.slab_major = slab_major;
   p.y = y;
   p.ldy = ldy;
-  p.counters = static_cast<int *>(workspace);
-  p.partials = reinterpret_cast<float *>(static_cast<char *>(workspace) + kCounterRegion);
+  p.counters = reinterpret_cast<int *>(static_cast<char *>(workspace) + kCounterOffset);
+  p.partials = reinterpret_cast<float *>(static_cast<char *>(workspace) + kPartialsOffset);
   p.status = status;
   const int smem = d.stages * stage_bytes_for(d.block_m) + static_cast<int>(sizeof(DecodeTail)) + 1024;
   // The attribute is set once per device to the most any plan may use.

@@ -22,9 +22,9 @@
 #include <cuda_runtime.h>
 #include <cudaTypedefs.h>
 
+#include <atomic>
 #include <cstdint>
 #include <cstring>
-#include <functional>
 #include <mutex>
 
 #include "decode_kernels.h"
@@ -40,9 +40,9 @@ constexpr int kMaxDevices = 64;
 static __device__ __align__(256) unsigned char g_decode_scratch[LLK_DECODE_NOALLOC_SCRATCH_BYTES];
 
 struct DeviceSetup {
-  std::once_flag once;
-  int status = LLK_ERR_DEVICE;  // outcome of the one-time set-up
-  void *scratch = nullptr;      // device address of g_decode_scratch on this device
+  std::mutex mu;
+  std::atomic<bool> ready{false};  // set once a set-up succeeded; a failed one is retried
+  void *scratch = nullptr;         // device address of g_decode_scratch on this device
   int sm_count = 0;
 };
 DeviceSetup g_setup[kMaxDevices];
@@ -52,44 +52,62 @@ std::mutex g_encode_mu;
 
 // One-time set-up for `dev`, which the caller has made current: the device
 // address of the scratch array, the SM count, the tensor-map encoder.
-void setup_device(int dev, DeviceSetup &s) {
+// Returns LLK_OK and marks the device ready, or an error and leaves it
+// unmarked so that a later call tries again.
+int setup_device(int dev, DeviceSetup &s) {
+  std::lock_guard<std::mutex> lk(s.mu);
+  if (s.ready) return LLK_OK;
   cudaDeviceProp prop;
-  if (cudaGetDeviceProperties(&prop, dev) != cudaSuccess || prop.major != 10 || prop.minor != 0) {
-    s.status = LLK_ERR_DEVICE;
-    return;
+  if (cudaGetDeviceProperties(&prop, dev) != cudaSuccess) {
+    cudaGetLastError();
+    return LLK_ERR_DEVICE;
   }
+  if (prop.major != 10 || prop.minor != 0) return LLK_ERR_DEVICE;
   void *ptr = nullptr;
   if (cudaGetSymbolAddress(&ptr, g_decode_scratch) != cudaSuccess || ptr == nullptr) {
     cudaGetLastError();
-    s.status = LLK_ERR_CUDA;
-    return;
+    return LLK_ERR_CUDA;
   }
   {
-    std::lock_guard<std::mutex> lk(g_encode_mu);
+    std::lock_guard<std::mutex> ek(g_encode_mu);
     if (!g_encode_fn) {
       void *fn = nullptr;
       cudaDriverEntryPointQueryResult q;
       if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &fn, cudaEnableDefault, &q) != cudaSuccess ||
           q != cudaDriverEntryPointSuccess || fn == nullptr) {
-        s.status = LLK_ERR_DEVICE;
-        return;
+        cudaGetLastError();
+        return LLK_ERR_DEVICE;
       }
       g_encode_fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(fn);
     }
   }
   s.scratch = ptr;
   s.sm_count = prop.multiProcessorCount;
-  s.status = LLK_OK;
+  s.ready = true;
+  return LLK_OK;
 }
 
-bool on_device(const void *p) {
+// Whether the kernel on `dev` may read / write p: device memory of `dev` or
+// managed memory.  Host memory (even pinned and mapped) is refused, since
+// staging it would need device memory; so is another GPU's memory, which the
+// kernel could only reach through peer access this call cannot vouch for.
+bool usable_on(const void *p, int dev) {
   cudaPointerAttributes a;
   if (p == nullptr || cudaPointerGetAttributes(&a, p) != cudaSuccess) {
     cudaGetLastError();
     return false;
   }
-  return a.type == cudaMemoryTypeDevice || a.type == cudaMemoryTypeManaged;
+  if (a.type == cudaMemoryTypeManaged) return true;
+  return a.type == cudaMemoryTypeDevice && a.device == dev;
 }
+
+// Restores the caller's current device when the call returns.
+struct DeviceGuard {
+  int prev = -1;
+  ~DeviceGuard() {
+    if (prev >= 0) cudaSetDevice(prev);
+  }
+};
 
 bool aligned16(const void *p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
@@ -114,35 +132,56 @@ extern "C" int llk_swiglu_decode_noalloc(const Tensor2D *x, const Tensor2D *wg, 
       y->dim1 != wg->dim1)
     return LLK_ERR_SHAPE;
   const int64_t M = x->dim0, K = x->dim1, N = wg->dim1;
-  if (M < 1 || K < 1 || N < 1 || !decode_supported(M, N, K, 0)) return LLK_ERR_UNSUPPORTED;
+  if (M < 1 || K < 1 || N < 1 || M > 128) return LLK_ERR_UNSUPPORTED;
   const int y_dtype = gpu ? gpu->y_dtype : LLK_DTYPE_BF16;
   if (y_dtype != LLK_DTYPE_BF16 && y_dtype != LLK_DTYPE_FP32) return LLK_ERR_ARG;
   const int y_f32 = y_dtype == LLK_DTYPE_FP32 ? 1 : 0;
 
-  // Scratch this shape needs; beyond the array's fixed size the call is refused.
-  if (decode_workspace_bytes(M, N, K, 0) > LLK_DECODE_NOALLOC_SCRATCH_BYTES) return LLK_ERR_NOMEM;
+  // The array's fixed size is the limit: the per-tile arrival counters
+  // (one int per 128 columns, up to N = LLK_DECODE_NOALLOC_MAX_N) and at
+  // least one CTA's partial-sum slots must fit.  Beyond that the call is
+  // refused, never allocated.
+  if (N > LLK_DECODE_NOALLOC_MAX_N || decode_max_grid_for(M, LLK_DECODE_NOALLOC_SCRATCH_BYTES) < 1)
+    return LLK_ERR_NOMEM;
+  if (!decode_supported(M, N, K, y_f32)) return LLK_ERR_UNSUPPORTED;
 
   int dev = gpu ? gpu->device : -1;
-  if (dev < 0 && cudaGetDevice(&dev) != cudaSuccess) return LLK_ERR_DEVICE;
-  if (dev >= kMaxDevices) return LLK_ERR_ARG;
   int cur = -1;
   if (cudaGetDevice(&cur) != cudaSuccess) return LLK_ERR_DEVICE;
-  if (cur != dev && cudaSetDevice(dev) != cudaSuccess) return LLK_ERR_DEVICE;
+  if (dev < 0) dev = cur;
+  if (dev >= kMaxDevices) return LLK_ERR_ARG;
+  DeviceGuard restore;
+  if (cur != dev) {
+    if (cudaSetDevice(dev) != cudaSuccess) {
+      cudaGetLastError();
+      return LLK_ERR_DEVICE;
+    }
+    restore.prev = cur;
+  }
   DeviceSetup &s = g_setup[dev];
-  std::call_once(s.once, setup_device, dev, std::ref(s));
-  if (s.status != LLK_OK) return s.status;
+  if (!s.ready) {
+    const int rc = setup_device(dev, s);
+    if (rc != LLK_OK) return rc;
+  }
 
-  // Device buffers only: staging host data would need device memory.
-  if (!on_device(x->data) || !on_device(wg->data) || !on_device(wu->data) || !on_device(y->data))
+  // Device buffers reachable from `dev` only: staging host data would need
+  // device memory, and a buffer on an unreachable GPU would fault the kernel.
+  if (!usable_on(x->data, dev) || !usable_on(wg->data, dev) || !usable_on(wu->data, dev) ||
+      !usable_on(y->data, dev))
     return LLK_ERR_ARG;
+  const uintptr_t y_align = y_f32 ? 4u : 2u;
   if (x->stride1 != 1 || wg->stride1 != 1 || wu->stride1 != 1 || y->stride1 != 1) return LLK_ERR_ALIGN;
   if (!aligned16(x->data) || !aligned16(wg->data) || !aligned16(wu->data) || (x->stride0 * 2) % 16 != 0 ||
       (wg->stride0 * 2) % 16 != 0 || (wu->stride0 * 2) % 16 != 0 || x->stride0 < K || wg->stride0 < N ||
-      wu->stride0 < N || y->stride0 < N)
+      wu->stride0 < N || y->stride0 < N || (reinterpret_cast<uintptr_t>(y->data) & (y_align - 1)) != 0)
     return LLK_ERR_ALIGN;
 
   cudaStream_t stream = gpu ? static_cast<cudaStream_t>(gpu->stream) : nullptr;
-  const DecodePlan d = decode_plan(M, N, K, s.sm_count);
+  DecodePlan d = decode_plan(M, N, K, s.sm_count);
+  // Fewer CTAs when the default grid's partial-sum slots would not fit the
+  // array (only for M > 32 with a split grid).
+  if (decode_workspace_bytes(M, N, K, d.grid) > LLK_DECODE_NOALLOC_SCRATCH_BYTES)
+    d.grid = decode_max_grid_for(M, LLK_DECODE_NOALLOC_SCRATCH_BYTES);
   CUtensorMap tg, tu, tx;
   if (!encode(&tg, wg->data, N, K, wg->stride0 * 2, 64, 64) ||
       !encode(&tu, wu->data, N, K, wu->stride0 * 2, 64, 64) ||

@@ -52,8 +52,18 @@ typedef struct MemRef2D {
 } MemRef2D;
 
 /* include/LLK/Runtime/JitCache.h:59-62.  `scratch` may point at DEVICE
- * memory the library may use as workspace (split-K partial sums); NULL
- * lets the library use its own per-device workspace. */
+ * memory the library may use as workspace (split-K partial sums, work
+ * counters); NULL lets the library use its own per-device workspace.
+ *
+ * Concurrency: the library workspace is one buffer per device.  Calls with
+ * device buffers return once their kernel is queued, so two calls that rely
+ * on it (decode-shaped SwiGLU, or prefill over 12 or more waves of tiles)
+ * and may overlap on the GPU -- different streams, or threads without
+ * ordering between them -- race on its counters and partial sums.  Serialise
+ * such calls per device (one stream, or events), or give each concurrent
+ * caller its own `scratch`.  After a kernel gives up a bounded wait
+ * (LLK_ERR_TIMEOUT), llk_synchronize clears the workspace as well as the
+ * status word, so later calls start from zeroed counters. */
 typedef struct KernelContext {
   void *scratch;
   size_t scratch_size;
@@ -146,8 +156,11 @@ int llk_diag_timeout_probe(int device, int64_t limit_ns);
 /* ---- decode without device allocation -------------------------------- */
 
 /* Size of the fixed device scratch array behind llk_swiglu_decode_noalloc
- * (16 MiB; every GPU that loads the library holds it until exit). */
+ * (16 MiB; every GPU that loads the library holds it until exit), and the
+ * widest N it serves (its per-tile arrival counters: one int per 128
+ * columns, 65536 of them). */
 #define LLK_DECODE_NOALLOC_SCRATCH_BYTES (16u << 20)
+#define LLK_DECODE_NOALLOC_MAX_N (65536ll * 128)
 
 /* The small-M (decode) fused SwiGLU for callers that cannot allocate device
  * memory: code whose GPU memory is owned by another allocator (e.g. a
@@ -161,21 +174,28 @@ int llk_diag_timeout_probe(int device, int64_t limit_ns);
  * split-K workspace is a fixed file-scope device array of
  * LLK_DECODE_NOALLOC_SCRATCH_BYTES, so the call allocates nothing: no
  * cudaMalloc/cudaFree, no library allocator.  The caller passes inputs and
- * outputs in DEVICE memory (host buffers are refused with LLK_ERR_ARG, as
- * staging them would need device memory).  Limits: 1 <= M <= 128, and the
- * workspace the shape needs, 262144 + ceil(N/128) * 4096 * Mp bytes (Mp = M
- * rounded up to 16, 32, 64 or 128), must fit the array; larger shapes are
- * refused with LLK_ERR_NOMEM.  Rows of X/Wg/Wu need 16-byte aligned starts
- * and pitches (else LLK_ERR_ALIGN).  Y is bf16, or f32 when
- * gpu->y_dtype == LLK_DTYPE_FP32.
+ * outputs in DEVICE memory of the call's device (or managed memory); host
+ * buffers and other GPUs' buffers are refused with LLK_ERR_ARG, as staging
+ * them would need device memory.  Limits: 1 <= M <= 128 (else
+ * LLK_ERR_UNSUPPORTED) and N <= LLK_DECODE_NOALLOC_MAX_N (else
+ * LLK_ERR_NOMEM: the array holds the counters of at most that many
+ * columns).  The workspace a launch needs is 256 KB + 256 bytes of counters
+ * plus, when CTAs share a column tile, 4096 * Mp bytes per CTA (Mp = M
+ * rounded up to 16, 32, 64 or 128); when the default grid's share would not
+ * fit, the call runs on fewer CTAs instead (possible only for M > 32).
+ * Rows of X/Wg/Wu need 16-byte aligned starts and pitches, Y a start
+ * aligned to its element size (else LLK_ERR_ALIGN).  Y is bf16, or f32
+ * when gpu->y_dtype == LLK_DTYPE_FP32.
  *
- * The first call on a device performs a one-time set-up with that device
- * current (it looks up the array's device address with
- * cudaGetSymbolAddress); make that first call before any stream capture.
- * Every call shares the one array and it keeps the last call's contents:
- * each call clears the counters that must start at zero.  Calls that overlap
- * on the GPU (different streams, or threads without ordering) race on the
- * array and corrupt each other's results -- serialise them.
+ * The first call on a device performs a set-up with that device current (it
+ * looks up the array's device address with cudaGetSymbolAddress); make that
+ * first call before any stream capture.  A set-up that fails is not
+ * remembered: the next call tries again.  The caller's current device is
+ * restored before the call returns.  Every call shares the one array and it
+ * keeps the last call's contents: each call clears the counters that must
+ * start at zero.  Calls that overlap on the GPU (different streams, or
+ * threads without ordering) race on the array and corrupt each other's
+ * results -- serialise them.
  *
  * device_status, if not NULL, is a device int that receives LLK_ERR_TIMEOUT
  * when a bounded wait in the kernel gives up (the call does not clear it).

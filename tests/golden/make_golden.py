@@ -4,7 +4,7 @@ by ``make -C oracle ref`` into oracle/_ref/ref_driver) on seeded inputs.
 
 Run here, where the reference tree exists:
 
-    make -C oracle ref && python tests/golden/make_golden.py
+    make -C oracle ref REF=<DSLCompiler tree> && python tests/golden/make_golden.py
 
 Each fixture holds bf16 inputs (uint16 bit patterns, drawn with
 dslcompiler_b200.datagen and rounded RNE), and the reference's outputs on
@@ -65,7 +65,7 @@ def run_reference(x, wg, wu):
 
 def main():
     if not os.path.exists(REF_DRIVER):
-        sys.exit("oracle/_ref/ref_driver missing: run `make -C oracle ref` where the reference tree exists")
+        sys.exit("oracle/_ref/ref_driver missing: run `make -C oracle ref REF=<DSLCompiler tree>` where the reference tree exists")
     for i, (name, M, N, K, std) in enumerate(CASES):
         x, wg, wu = dg.swiglu_inputs(M, K, N, std, std, seed=1000 + i)
         y32, y64 = run_reference(x, wg, wu)

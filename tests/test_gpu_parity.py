@@ -366,7 +366,11 @@ def test_probe_reports_b200():
 # ------------------------------------------------------------ decode kernel
 @pytest.mark.parametrize("M,K,N", [(1, 4096, 14336), (4, 4096, 14336), (16, 4096, 14336), (3, 512, 200),
                                    (17, 1024, 1000), (64, 2048, 4096), (100, 256, 384), (128, 1024, 1536),
-                                   (1, 64, 128), (7, 4104, 136)])
+                                   (1, 64, 128), (7, 4104, 136),
+                                   # 8-way column shards of config 4 (14 and 13 tiles over every SM:
+                                   # ~10 contributors per tile)
+                                   (1, 4096, 1792), (4, 4096, 1792), (16, 4096, 1792), (1, 4096, 1664),
+                                   (4, 4096, 1664), (16, 4096, 1664), (2, 4096, 3584), (33, 8192, 256)])
 def test_decode_vs_oracle(M, K, N):
     x, wg, wu = dg.swiglu_inputs(M, K, N, 1.0, 0.02, seed=M * 7 + N)
     y = llk.fused_swiglu(dev(x), dev(wg), dev(wu), out_dtype="f32", variant="decode")

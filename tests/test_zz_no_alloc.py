@@ -65,6 +65,24 @@ def test_noalloc_matches_existing_entry_point_twice(M, K, N):
         assert (y - ref).abs().max().item() <= TOL_F32 * scale
 
 
+def test_noalloc_stream_k_shape_vs_oracle():
+    """A shape whose column tiles are shared by several CTAs (8 tiles x 16
+    k-blocks over every SM), so the partial-sum slots in the fixed array are
+    used: checked against the CPU oracle directly, twice."""
+    import oracle
+
+    M, K, N = 5, 1024, 1000
+    x, wg, wu = dg.swiglu_inputs(M, K, N, 1.0, 0.02, seed=77)
+    ref = oracle.swiglu_fused(x, wg, wu, "f32").astype(np.float64)
+    xd, gd, ud = dev(x), dev(wg), dev(wu)
+    for _ in range(2):
+        y = torch.full((M, N), float("nan"), dtype=torch.float32, device="cuda")
+        assert noalloc(xd, gd, ud, y) == capi.LLK_OK
+        torch.cuda.synchronize()
+        err = np.abs(y.cpu().numpy().astype(np.float64) - ref).max() / np.abs(ref).max()
+        assert err <= TOL_F32
+
+
 def test_noalloc_bf16_output_and_limits():
     x, wg, wu = dg.swiglu_inputs(4, 512, 640, 1.0, 0.02, seed=3)
     xd, gd, ud = dev(x), dev(wg), dev(wu)
@@ -74,12 +92,36 @@ def test_noalloc_bf16_output_and_limits():
         assert noalloc(xd, gd, ud, y) == capi.LLK_OK
         torch.cuda.synchronize()
         assert (y.float() - ref.float()).abs().max().item() <= TOL_BF16 * ref.float().abs().max().item()
-    # a shape whose workspace exceeds the fixed array is refused, not allocated
-    big_n = 128 * 40
-    xb = torch.zeros((128, 64), dtype=torch.bfloat16, device="cuda")
-    wb = torch.zeros((64, big_n), dtype=torch.bfloat16, device="cuda")
-    yb = torch.empty((128, big_n), dtype=torch.bfloat16, device="cuda")
-    assert noalloc(xb, wb, wb, yb) == capi.LLK_ERR_NOMEM
+    # wider than the fixed array's counters: refused with LLK_ERR_NOMEM before
+    # any buffer is touched (the descriptors claim more columns than exist)
+    tx, ty = llk.tensor2d(xd), llk.tensor2d(y)
+    big = capi.LLK_DECODE_NOALLOC_MAX_N + 128
+    tw = capi.Tensor2D(gd.data_ptr(), 512, big, big, 1)
+    ty = capi.Tensor2D(y.data_ptr(), 4, big, big, 1)
+    g = capi.GpuContext()
+    g.device = torch.cuda.current_device()
+    g.stream = torch.cuda.current_stream().cuda_stream
+    rc = capi.lib().llk_swiglu_decode_noalloc(ctypes.byref(tx), ctypes.byref(tw), ctypes.byref(tw),
+                                              ctypes.byref(ty), None, ctypes.byref(g))
+    assert rc == capi.LLK_ERR_NOMEM
     # host buffers would need staging memory: refused
     xh = np.zeros((4, 512), np.uint16)
     assert noalloc(xh, gd, ud, y) == capi.LLK_ERR_ARG
+    # a Y start not aligned to its element size: refused, not faulted
+    raw = torch.empty((4 * 640 * 2 + 16,), dtype=torch.uint8, device="cuda")
+    ty_bad = capi.Tensor2D(raw.data_ptr() + 1, 4, 640, 640, 1)
+    g.y_dtype = capi.LLK_DTYPE_BF16
+    tg, tu = llk.tensor2d(gd), llk.tensor2d(ud)
+    rc = capi.lib().llk_swiglu_decode_noalloc(ctypes.byref(tx), ctypes.byref(tg), ctypes.byref(tu),
+                                              ctypes.byref(ty_bad), None, ctypes.byref(g))
+    assert rc == capi.LLK_ERR_ALIGN
+
+
+def test_noalloc_leaves_current_device_alone():
+    x, wg, wu = dg.swiglu_inputs(2, 256, 256, 1.0, 0.02, seed=9)
+    xd, gd, ud = dev(x), dev(wg), dev(wu)
+    y = torch.empty((2, 256), dtype=torch.float32, device="cuda")
+    before = torch.cuda.current_device()
+    assert noalloc(xd, gd, ud, y) == capi.LLK_OK
+    torch.cuda.synchronize()
+    assert torch.cuda.current_device() == before
