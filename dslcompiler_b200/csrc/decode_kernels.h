@@ -11,6 +11,11 @@ namespace llk_b200 {
 
 struct DecodePlan {
   int block_m, block_n, block_k, stages, split_k, grid, threads, smem_bytes;
+  // 0: stream-K split of the (tile, k-block) units over `grid` CTAs,
+  // partial sums through the workspace.  s >= 2: grid = tiles x s CTAs in
+  // clusters of s, one cluster per tile, partial sums through distributed
+  // shared memory.
+  int cluster;
 };
 
 // Largest M the decode kernel serves.
@@ -18,10 +23,10 @@ int decode_max_m();
 // Whether the decode kernel handles this shape / output type.
 bool decode_supported(int64_t M, int64_t N, int64_t K, int y_f32);
 DecodePlan decode_plan(int64_t M, int64_t N, int64_t K, int sm_count);
-// Device workspace a launch of `grid` CTAs needs: 256 bytes reserved for the
-// CTA-pair kernel's work counter, the per-tile arrival counters, and (when
-// some CTA's range starts inside a tile) two partial-sum slots per CTA.
-size_t decode_workspace_bytes(int64_t M, int64_t N, int64_t K, int grid);
+// Device workspace a launch of plan d needs (layout in workspace.h): the
+// counter regions, and for a stream-K plan whose CTA ranges start inside
+// tiles two partial-sum slots per CTA.
+size_t decode_workspace_bytes(int64_t M, int64_t N, int64_t K, const DecodePlan &d);
 // Largest grid whose partial-sum slots fit in `workspace_bytes`.
 int decode_max_grid_for(int64_t M, size_t workspace_bytes);
 // Byte offset and size of the per-tile counters inside the workspace; they

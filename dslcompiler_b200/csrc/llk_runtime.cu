@@ -23,6 +23,7 @@
 #include "decode_kernels.h"
 #include "llk_b200.h"
 #include "tc_kernels.h"
+#include "workspace.h"
 
 using namespace llk_b200;
 
@@ -279,6 +280,7 @@ llk_launch_plan build_plan(int variant, int op, int64_t M, int64_t N, int64_t K,
     p.grid = d.grid;
     p.threads = d.threads;
     p.smem_bytes = d.smem_bytes;
+    p.sched = d.cluster ? 1 : 0;  // decode: 1 = one cluster of split_k CTAs per tile
   } else {
     p.block_m = 1;
     p.block_n = 256;
@@ -374,10 +376,10 @@ int launch_device(DeviceState &ds, int op, const DevTensor &x, const DevTensor &
   }
 
   if (variant == LLK_VARIANT_DECODE) {
-    DecodePlan d = {plan.block_m, plan.block_n, plan.block_k, plan.stages, plan.split_k, plan.grid, plan.threads,
-                     plan.smem_bytes};
+    DecodePlan d = {plan.block_m, plan.block_n, plan.block_k, plan.stages,   plan.split_k,
+                    plan.grid,    plan.threads, plan.smem_bytes, plan.sched ? plan.split_k : 0};
     if (!decode_plan_valid(M, N, K, d)) d = decode_plan(M, N, K, ds.sm_count);
-    const size_t need = decode_workspace_bytes(M, N, K, d.grid);
+    const size_t need = decode_workspace_bytes(M, N, K, d);
     void *ws = scratch;
     if (ws != nullptr) {
       // Caller scratch: its tile counters start from an unknown state.
@@ -434,28 +436,43 @@ int launch_device(DeviceState &ds, int op, const DevTensor &x, const DevTensor &
   p.slab_major = slab ? 1 : 0;
   if (pair) {
     const int max_pairs = plan.variant == LLK_VARIANT_TC && plan.grid >= 2 ? plan.grid / 2 : 0;
-    // plan.split_k for the pair kernel: N-split of the leftover tiles (0 = choose).
+    // plan.split_k for the pair kernel: tail split of the leftover tiles (0 = choose,
+    // 1/2/4 = that many column parts, -s = s K parts).
     const int tail_split = plan.variant == LLK_VARIANT_TC ? plan.split_k : 0;
-    // Dynamic work distribution needs one zeroed device int: the caller's
-    // scratch (cleared here) or the library workspace (kept at zero by every
-    // launch).  plan.sched = 1 selects the static schedule.
-    int *counter = nullptr;
-    if (plan.variant == LLK_VARIANT_TC && plan.sched == 0) {
-      if (scratch != nullptr) {
-        if (scratch_bytes < kTc2SchedBytes) return LLK_ERR_NOMEM;
+    // The workspace: the library's (counter regions kept at zero by every
+    // launch) or the caller's scratch, whose counter regions are cleared
+    // here.  It holds the dynamic schedule's work counter (plan.sched = 0;
+    // 1 selects the static schedule) and the K-split tail's counters and
+    // partial sums.
+    const bool dynamic = plan.variant == LLK_VARIANT_TC && plan.sched == 0;
+    void *ws = nullptr;
+    size_t ws_bytes = 0;
+    if (scratch != nullptr) {
+      if (scratch_bytes >= kWsTc2CounterBytes) {
+        if (cudaMemsetAsync(scratch, 0, kWsTc2CounterBytes, stream) != cudaSuccess) return LLK_ERR_CUDA;
+        ws = scratch;
+        ws_bytes = scratch_bytes;
+      } else if (scratch_bytes >= kTc2SchedBytes) {
+        // room for the work counter only (no K-split tail)
         if (cudaMemsetAsync(scratch, 0, sizeof(int), stream) != cudaSuccess) return LLK_ERR_CUDA;
-        counter = static_cast<int *>(scratch);
-      } else {
-        if (ds.workspace.ensure(kTc2SchedBytes, true) != cudaSuccess) return LLK_ERR_NOMEM;
-        counter = static_cast<int *>(ds.workspace.ptr);
+        ws = scratch;
+        ws_bytes = 0;
+      } else if (dynamic) {
+        return LLK_ERR_NOMEM;
       }
+    } else {
+      if (ds.workspace.ensure(tc2_tail_workspace_bytes(ds.sm_count), true) != cudaSuccess) return LLK_ERR_NOMEM;
+      ws = ds.workspace.ptr;
+      ws_bytes = ds.workspace.bytes;
     }
+    int *counter = dynamic ? reinterpret_cast<int *>(static_cast<char *>(ws) + kWsTc2Counters) : nullptr;
     if (peers) {
       p.n_peers = peers->n;
       for (int i = 0; i < peers->n; ++i) p.y_peers[i] = peers->y[i];
       if (peers_done) *peers_done = true;
     }
-    e = tc2_launch(mode, ta, tb0, tb1, p, max_pairs, tail_split, counter, stream, peers ? peers->maps : nullptr);
+    e = tc2_launch(mode, ta, tb0, tb1, p, max_pairs, tail_split, counter, ws_bytes ? ws : nullptr, ws_bytes, stream,
+                   peers ? peers->maps : nullptr);
     return e == cudaSuccess ? LLK_OK : LLK_ERR_CUDA;
   }
   int grid = p.num_tiles < ds.sm_count ? p.num_tiles : ds.sm_count;

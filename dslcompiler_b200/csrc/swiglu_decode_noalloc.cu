@@ -178,9 +178,9 @@ extern "C" int llk_swiglu_decode_noalloc(const Tensor2D *x, const Tensor2D *wg, 
 
   cudaStream_t stream = gpu ? static_cast<cudaStream_t>(gpu->stream) : nullptr;
   DecodePlan d = decode_plan(M, N, K, s.sm_count);
-  // Fewer CTAs when the default grid's partial-sum slots would not fit the
-  // array (only for M > 32 with a split grid).
-  if (decode_workspace_bytes(M, N, K, d.grid) > LLK_DECODE_NOALLOC_SCRATCH_BYTES)
+  // Fewer CTAs when a stream-K grid's partial-sum slots would not fit the
+  // array (only for M > 32).
+  if (decode_workspace_bytes(M, N, K, d) > LLK_DECODE_NOALLOC_SCRATCH_BYTES)
     d.grid = decode_max_grid_for(M, LLK_DECODE_NOALLOC_SCRATCH_BYTES);
   CUtensorMap tg, tu, tx;
   if (!encode(&tg, wg->data, N, K, wg->stride0 * 2, 64, 64) ||

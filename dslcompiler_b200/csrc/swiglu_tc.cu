@@ -97,6 +97,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
+  pdl_launch_dependents();
+  pdl_wait();  // the previous kernel's writes are visible from here on
   const uint32_t tmem_base = st->tmem_base;
   volatile int *abort = &st->abort;
 
@@ -320,7 +322,20 @@ static cudaError_t launch_mode(const CUtensorMap &a, const CUtensorMap &b0, cons
     if (e != cudaSuccess) return e;
     attr_set.fetch_or(bit);
   }
-  kern<<<grid, kThreads, smem, stream>>>(a, b0, b1, p);
+  // Programmatic stream serialisation: CTAs may start and set up while the
+  // previous kernel finishes (the kernel waits for it: pdl_wait).
+  cudaLaunchConfig_t cfg = {};
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.gridDim = dim3(grid);
+  cfg.blockDim = dim3(kThreads);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  cudaError_t e = cudaLaunchKernelEx(&cfg, kern, a, b0, b1, p);
+  if (e != cudaSuccess) return e;
   return cudaGetLastError();
 }
 

@@ -40,6 +40,7 @@
 
 #include "sm100_ptx.cuh"
 #include "tc_kernels.h"
+#include "workspace.h"
 
 namespace llk_b200 {
 
@@ -61,28 +62,206 @@ constexpr uint32_t kStagingPerWarp = 8192;
 constexpr uint32_t kStagingBytes = 4 * kStagingPerWarp;
 constexpr uint64_t kWaitLimitNs = 2000000000ull;
 
-// One unit of a pair's work: Y columns [c0, c0 + wn) of tile `tile`.
+// One unit of a pair's work: Y columns [c0, c0 + wn) of tile `tile`, over
+// the k-blocks [kb0, kb1); part `part` of `nparts` K parts of the tile
+// (nparts = 1: the whole reduction).
 struct Work {
   int tile, c0, wn;
+  int kb0, kb1, part, nparts;
 };
 
 // Work item `item` of the launch: items [0, whole) are whole tiles (whole =
-// dp_waves x pairs), the rest are the tail_split column parts of the
-// leftover tiles.  False past the last item.
+// dp_waves x pairs), the rest are the parts of the leftover tiles: ksplit
+// K parts each, or else tail_split column parts.  False past the last item.
 template <int TILE_N>
 __device__ __forceinline__ bool item_to_work(const TcParams &p, int n_pairs, int item, Work &w) {
   const int whole = p.dp_waves * n_pairs;
+  w.c0 = 0;
+  w.wn = TILE_N;
+  w.kb0 = 0;
+  w.kb1 = p.k_blocks;
+  w.part = 0;
+  w.nparts = 1;
   if (item < whole) {
     w.tile = item;
-    w.c0 = 0;
-    w.wn = TILE_N;
     return true;
   }
   const int j = item - whole;
+  if (p.ksplit > 1) {
+    if (j >= (p.num_tiles - whole) * p.ksplit) return false;
+    w.tile = whole + j / p.ksplit;
+    w.part = j % p.ksplit;
+    w.nparts = p.ksplit;
+    w.kb0 = w.part * p.k_blocks / p.ksplit;
+    w.kb1 = (w.part + 1) * p.k_blocks / p.ksplit;
+    return true;
+  }
   if (j >= (p.num_tiles - whole) * p.tail_split) return false;
   w.tile = whole + j / p.tail_split;
   w.wn = TILE_N / p.tail_split;
   w.c0 = (j % p.tail_split) * w.wn;
+  return true;
+}
+
+// Epilogue of one K part of a K-split leftover tile, for one epilogue warp
+// (TMEM lane quarter q = rows q*32 .. q*32+31 of this CTA's 128).  The
+// accumulator columns are cut into 16-column chunks of Y (SwiGLU: gate and
+// up columns of those Y columns; matmul: C columns), chunk c owned by part
+// c % nparts.  1. Write the chunks this part does not own to its partial
+// block.  2. Publish (fence + counter) and wait, bounded, until every part
+// of the tile has.  3. For each owned chunk, add the parts' sums in part
+// order -- this part's straight from TMEM -- and run the epilogue.  4. The
+// last part to get here sets the tile's counters back to zero.
+// Partial block of (leftover tile, part, CTA rank): 64 float4 columns x 128
+// rows, float4-column-major, so a warp's 32 rows of one float4 column are
+// 512 contiguous bytes.  Returns false when the wait gave up.
+template <int MODE>
+__device__ __forceinline__ bool ksplit_epilogue(const TcParams &p, const Work &w, int tl, uint32_t rank, int q,
+                                                int lane, uint32_t t_row, int m0, int n0, volatile int *abort) {
+  constexpr bool kSwiglu = (MODE == TC_SWIGLU_BF16 || MODE == TC_SWIGLU_F32);
+  constexpr int kChunks = kSwiglu ? 8 : 16;
+  constexpr size_t kBlock = 64 * 128;  // float4s per partial block
+  const int s = w.nparts;
+  const int r = q * 32 + lane;
+  float4 *const tail = reinterpret_cast<float4 *>(p.tail_ws);
+  const size_t tile_base = (size_t)tl * s * 2;
+  float4 *mine = tail + ((tile_base + w.part * 2 + rank) * kBlock);
+#pragma unroll 1
+  for (int c = 0; c < kChunks; ++c) {
+    if (c % s == w.part) continue;
+    uint32_t a[16];
+    tmem_ld_32x32b_x16(t_row + 16 * c, a);
+    if (kSwiglu) {
+      uint32_t b[16];
+      tmem_ld_32x32b_x16(t_row + 128 + 16 * c, b);
+      tmem_ld_wait();
+#pragma unroll
+      for (int i = 0; i < 4; ++i)
+        mine[(size_t)(32 + 4 * c + i) * 128 + r] = make_float4(__uint_as_float(b[4 * i]), __uint_as_float(b[4 * i + 1]),
+                                                               __uint_as_float(b[4 * i + 2]),
+                                                               __uint_as_float(b[4 * i + 3]));
+    } else {
+      tmem_ld_wait();
+    }
+#pragma unroll
+    for (int i = 0; i < 4; ++i)
+      mine[(size_t)(4 * c + i) * 128 + r] = make_float4(__uint_as_float(a[4 * i]), __uint_as_float(a[4 * i + 1]),
+                                                        __uint_as_float(a[4 * i + 2]), __uint_as_float(a[4 * i + 3]));
+  }
+  __threadfence();
+  __syncwarp();
+  int *cnt = p.tail_cnt + ((tl * 2 + static_cast<int>(rank)) * 4 + q) * 2;
+  int ok = 1;
+  if (lane == 0) {
+    atomicAdd(cnt, 1);
+    const uint64_t t0 = global_timer_ns();
+    for (uint32_t i = 1; ld_acquire_gpu(cnt) < s; ++i) {
+      if ((i & 63u) == 0) {
+        if (*abort != 0) {
+          ok = 0;
+          break;
+        }
+        if (global_timer_ns() - t0 > kWaitLimitNs) {
+          *abort = LLK_ERR_TIMEOUT;
+          ok = 0;
+          break;
+        }
+      }
+    }
+  }
+  ok = __shfl_sync(0xffffffffu, ok, 0);
+  if (!ok) return false;
+  __threadfence();
+  const int row = m0 + r;
+#pragma unroll 1
+  for (int c = w.part; c < kChunks; c += s) {
+    uint32_t a[16], b[16];
+    tmem_ld_32x32b_x16(t_row + 16 * c, a);
+    if (kSwiglu) tmem_ld_32x32b_x16(t_row + 128 + 16 * c, b);
+    tmem_ld_wait();
+    float ga[16], ua[16];
+#pragma unroll
+    for (int j = 0; j < 16; ++j) ga[j] = ua[j] = 0.f;
+    for (int part = 0; part < s; ++part) {
+      if (part == w.part) {
+#pragma unroll
+        for (int j = 0; j < 16; ++j) {
+          ga[j] += __uint_as_float(a[j]);
+          if (kSwiglu) ua[j] += __uint_as_float(b[j]);
+        }
+      } else {
+        const float4 *pb = tail + ((tile_base + part * 2 + rank) * kBlock) + r;
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          const float4 v = __ldcg(pb + (size_t)(4 * c + i) * 128);
+          ga[4 * i] += v.x;
+          ga[4 * i + 1] += v.y;
+          ga[4 * i + 2] += v.z;
+          ga[4 * i + 3] += v.w;
+          if (kSwiglu) {
+            const float4 u = __ldcg(pb + (size_t)(32 + 4 * c + i) * 128);
+            ua[4 * i] += u.x;
+            ua[4 * i + 1] += u.y;
+            ua[4 * i + 2] += u.z;
+            ua[4 * i + 3] += u.w;
+          }
+        }
+      }
+    }
+    const int col = n0 + 16 * c;
+    if (row >= p.M || col >= p.N) continue;
+    const int64_t off = (int64_t)row * p.ldy + col;
+    const bool vec = p.vec_ok && col + 16 <= p.N;
+    if (kSwiglu) {
+      float y[16];
+#pragma unroll
+      for (int j = 0; j < 16; ++j) y[j] = silu_mul(ga[j], ua[j]);
+      for (int t = -1; t < p.n_peers; ++t) {
+        void *base = t < 0 ? p.y : p.y_peers[t];
+        if (MODE == TC_SWIGLU_BF16) {
+          uint16_t *dst = reinterpret_cast<uint16_t *>(base) + off;
+          if (vec) {
+            uint4 *d4 = reinterpret_cast<uint4 *>(dst);
+            d4[0] = make_uint4(pack_bf16x2(y[0], y[1]), pack_bf16x2(y[2], y[3]), pack_bf16x2(y[4], y[5]),
+                               pack_bf16x2(y[6], y[7]));
+            d4[1] = make_uint4(pack_bf16x2(y[8], y[9]), pack_bf16x2(y[10], y[11]), pack_bf16x2(y[12], y[13]),
+                               pack_bf16x2(y[14], y[15]));
+          } else {
+#pragma unroll
+            for (int j = 0; j < 16; ++j)
+              if (col + j < p.N) dst[j] = static_cast<uint16_t>(pack_bf16x2(y[j], 0.f));
+          }
+        } else {
+          float *dst = reinterpret_cast<float *>(base) + off;
+          if (vec) {
+            float4 *d4 = reinterpret_cast<float4 *>(dst);
+#pragma unroll
+            for (int v = 0; v < 4; ++v) d4[v] = make_float4(y[4 * v], y[4 * v + 1], y[4 * v + 2], y[4 * v + 3]);
+          } else {
+#pragma unroll
+            for (int j = 0; j < 16; ++j)
+              if (col + j < p.N) dst[j] = y[j];
+          }
+        }
+      }
+    } else {
+      float *dst = reinterpret_cast<float *>(p.y) + off;
+#pragma unroll
+      for (int j = 0; j < 16; ++j) {
+        if (col + j < p.N) {
+          float o = ga[j];
+          if (MODE == TC_MATMUL_F32_ACC) o += dst[j];
+          dst[j] = o;
+          for (int t = 0; t < p.n_peers; ++t) reinterpret_cast<float *>(p.y_peers[t])[off + j] = o;
+        }
+      }
+    }
+  }
+  __syncwarp();
+  if (lane == 0 && atomicAdd(cnt + 1, 1) == s - 1) {
+    atomicExch(cnt, 0);
+    atomicExch(cnt + 1, 0);
+  }
   return true;
 }
 
@@ -237,6 +416,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   __syncthreads();
   cluster_sync_all();  // the peer may only signal the leader's barriers once they exist
   tc_fence_after();
+  pdl_launch_dependents();
+  pdl_wait();  // the previous kernel's writes (X, W, the workspace) are visible from here on
   const uint32_t tmem_base = st->tmem_base;
   volatile int *abort = &st->abort;
 
@@ -264,7 +445,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int nb = kSwiglu ? n0 : n0 + static_cast<int>(rank) * cta_cols;
         const int slabs = cta_cols > 64 ? 2 : 1;
         const uint32_t stage_tx = 2u * (kABytes + slabs * kSlabBytes);
-        for (int kb = 0; kb < p.k_blocks; ++kb) {
+        for (int kb = w.kb0; kb < w.kb1; ++kb) {
           if (!mbar_wait_bounded(&st->empty[stage], phase ^ 1u, abort, LLK_ERR_TIMEOUT, kWaitLimitNs)) {
             ok = false;
             break;
@@ -329,7 +510,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + acc * kMmaN;
-        for (int kb = 0; kb < p.k_blocks; ++kb) {
+        for (int kb = w.kb0; kb < w.kb1; ++kb) {
           if (!mbar_wait_bounded(&st->full[stage], phase, abort, LLK_ERR_TIMEOUT, kWaitLimitNs)) {
             ok = false;
             break;
@@ -341,7 +522,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           for (int kk = 0; kk < kBK / 16; ++kk) {
             const uint64_t a_desc = make_smem_desc_sw128(a_addr + kk * 32, 16, 1024);
             const uint64_t b_desc = make_smem_desc_sw128(b_addr + kk * 2048, kSlabBytes, 1024);
-            tc_mma_bf16_pair(d_tmem, a_desc, b_desc, idesc, (kb > 0 || kk > 0) ? 1u : 0u);
+            tc_mma_bf16_pair(d_tmem, a_desc, b_desc, idesc, (kb > w.kb0 || kk > 0) ? 1u : 0u);
           }
           tc_commit_pair_mc(&st->empty[stage], 0x3);
           if (++stage == kStages) {
@@ -378,7 +559,12 @@ __global__ void __launch_bounds__(kThreads, 1)
       const int n0 = nt * kTileN + w.c0;
       const int row = m0 + row_in_tile;
       const uint32_t t_row = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + acc * kMmaN;
-      if (kSwiglu && ym.n > 0) {
+      if (w.nparts > 1) {
+        if (!ksplit_epilogue<MODE>(p, w, w.tile - p.dp_waves * n_pairs, rank, q, lane, t_row, m0, n0, abort)) {
+          ok = false;
+          break;
+        }
+      } else if (kSwiglu && ym.n > 0) {
         // Staged TMA stores: lane = row; the chunk goes to shared memory in
         // the map's swizzled layout (64-byte rows for bf16, 128-byte for
         // f32; the XOR keeps each 8-lane phase of the 16-byte stores on
@@ -564,24 +750,35 @@ int resident_pairs() {
   return clusters;
 }
 
+// Partial-sum bytes of the K-split tail: one 128-row x 256-column f32 block
+// per (leftover tile, part, CTA of the pair).
+constexpr size_t kTailBlockBytes = 128 * 256 * sizeof(float);
+// Tail counters available in the workspace's counter region (two per
+// leftover tile, CTA and epilogue warp).
+constexpr int kMaxTailTiles = static_cast<int>((kWsTc2CounterBytes - kWsTc2TailCounters) / (2 * 4 * 2 * sizeof(int)));
+
 template <int MODE>
 cudaError_t launch_pair_mode(const CUtensorMap &a, const CUtensorMap &b0, const CUtensorMap &b1, TcParams p,
-                             int max_pairs, int tail_split, int *sched_counter, cudaStream_t stream,
-                             const YStoreMaps &ym) {
+                             int max_pairs, int tail_split, int *sched_counter, void *workspace,
+                             size_t workspace_bytes, cudaStream_t stream, const YStoreMaps &ym) {
   auto kern = tc2_kernel<MODE>;
   const int clusters = resident_pairs<MODE>();
   if (clusters < 1) return cudaErrorInvalidValue;
   cudaLaunchConfig_t cfg = {};
-  cudaLaunchAttribute attr[1];
+  cudaLaunchAttribute attr[2];
   attr[0].id = cudaLaunchAttributeClusterDimension;
   attr[0].val.clusterDim.x = 2;
   attr[0].val.clusterDim.y = 1;
   attr[0].val.clusterDim.z = 1;
+  // CTAs may start and set up while the previous kernel finishes; the kernel
+  // waits for it before its first memory access (pdl_wait).
+  attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[1].val.programmaticStreamSerializationAllowed = 1;
   cfg.blockDim = dim3(kThreads);
   cfg.dynamicSmemBytes = tc2_smem_bytes();
   cfg.stream = stream;
   cfg.attrs = attr;
-  cfg.numAttrs = 1;
+  cfg.numAttrs = 2;
   cudaError_t e = cudaSuccess;
   int pairs = clusters;
   if (max_pairs >= 1 && pairs > max_pairs) pairs = max_pairs;
@@ -596,11 +793,24 @@ cudaError_t launch_pair_mode(const CUtensorMap &a, const CUtensorMap &b0, const 
   // and measured slower on every shape tried (8-GPU config-3 shard: 93 us
   // against 50 us): re-reading 128 KB of f32 rows per part costs more than
   // the shorter wave saves.
+  //
+  // Or, with the static schedule and room in the workspace, the leftover
+  // tiles are cut along K into s = pairs / left parts (at most 8), one per
+  // pair: a part costs 1/s of a tile plus its share of the partial-sum
+  // exchange, charged 0.12 of a tile (each CTA writes and reads about
+  // (s-1)/s x 128 KB through L2).
   p.group_m = kBandBlocks < p.m_tiles ? kBandBlocks : p.m_tiles;
   p.dp_waves = p.num_tiles / pairs;
   const int left = p.num_tiles - p.dp_waves * pairs;
-  int g = 1;
-  if (tail_split == 1 || tail_split == 2 || tail_split == 4) {
+  auto ksplit_fits = [&](int ks) {
+    return ks >= 2 && ks <= 8 && ks <= p.k_blocks && left > 0 && left * ks <= pairs && left <= kMaxTailTiles &&
+           sched_counter == nullptr && workspace != nullptr &&
+           workspace_bytes >= kWsPartials + static_cast<size_t>(left) * ks * 2 * kTailBlockBytes;
+  };
+  int g = 1, ks = 0;
+  if (tail_split < 0 && ksplit_fits(-tail_split)) {
+    ks = -tail_split;
+  } else if (tail_split == 1 || tail_split == 2 || tail_split == 4) {
     g = tail_split;
   } else if (left > 0) {
     double best = 1e30;
@@ -611,11 +821,21 @@ cudaError_t launch_pair_mode(const CUtensorMap &a, const CUtensorMap &b0, const 
         g = cand;
       }
     }
+    int cand = pairs / left;
+    if (cand > 8) cand = 8;
+    if (cand > p.k_blocks) cand = p.k_blocks;
+    if (ksplit_fits(cand) && 1.0 / cand + 0.12 < best - 1e-9) ks = cand;
   }
-  p.tail_split = g;
+  p.ksplit = ks;
+  p.tail_split = ks ? 1 : g;
+  const int parts = ks ? ks : g;
+  if (ks) {
+    p.tail_ws = reinterpret_cast<float *>(static_cast<char *>(workspace) + kWsPartials);
+    p.tail_cnt = reinterpret_cast<int *>(static_cast<char *>(workspace) + kWsTc2TailCounters);
+  }
   // No pair without work: at most all tiles' parts.
-  if (p.dp_waves == 0 && pairs > left * g) pairs = left * g;
-  p.n_items = p.dp_waves * pairs + left * g;
+  if (p.dp_waves == 0 && pairs > left * parts) pairs = left * parts;
+  p.n_items = p.dp_waves * pairs + left * parts;
   p.dynamic = sched_counter != nullptr ? 1 : 0;
   p.sched_counter = sched_counter;
   cfg.gridDim = dim3(2 * pairs);
@@ -630,19 +850,28 @@ int tc2_smem_bytes() { return kStages * kStageBytes + kStagingBytes + static_cas
 static_assert(kStages * kStageBytes + kStagingBytes + sizeof(PairTail) + 1024 <= 227 * 1024,
               "CTA-pair kernel shared memory over the 227 KB opt-in limit");
 
+size_t tc2_tail_workspace_bytes(int sm_count) {
+  return kWsPartials + static_cast<size_t>(sm_count / 2) * 2 * kTailBlockBytes;
+}
+
 cudaError_t tc2_launch(int mode, const CUtensorMap &a, const CUtensorMap &b0, const CUtensorMap &b1, TcParams p,
-                       int max_pairs, int tail_split, int *sched_counter, cudaStream_t stream, const YStoreMaps *ym) {
+                       int max_pairs, int tail_split, int *sched_counter, void *workspace, size_t workspace_bytes,
+                       cudaStream_t stream, const YStoreMaps *ym) {
   static const YStoreMaps kNoMaps = {};
   const YStoreMaps &m = ym ? *ym : kNoMaps;
   switch (mode) {
     case TC_SWIGLU_BF16:
-      return launch_pair_mode<TC_SWIGLU_BF16>(a, b0, b1, p, max_pairs, tail_split, sched_counter, stream, m);
+      return launch_pair_mode<TC_SWIGLU_BF16>(a, b0, b1, p, max_pairs, tail_split, sched_counter, workspace,
+                                              workspace_bytes, stream, m);
     case TC_SWIGLU_F32:
-      return launch_pair_mode<TC_SWIGLU_F32>(a, b0, b1, p, max_pairs, tail_split, sched_counter, stream, m);
+      return launch_pair_mode<TC_SWIGLU_F32>(a, b0, b1, p, max_pairs, tail_split, sched_counter, workspace,
+                                             workspace_bytes, stream, m);
     case TC_MATMUL_F32:
-      return launch_pair_mode<TC_MATMUL_F32>(a, b0, b1, p, max_pairs, tail_split, sched_counter, stream, kNoMaps);
+      return launch_pair_mode<TC_MATMUL_F32>(a, b0, b1, p, max_pairs, tail_split, sched_counter, workspace,
+                                             workspace_bytes, stream, kNoMaps);
     case TC_MATMUL_F32_ACC:
-      return launch_pair_mode<TC_MATMUL_F32_ACC>(a, b0, b1, p, max_pairs, tail_split, sched_counter, stream, kNoMaps);
+      return launch_pair_mode<TC_MATMUL_F32_ACC>(a, b0, b1, p, max_pairs, tail_split, sched_counter, workspace,
+                                                 workspace_bytes, stream, kNoMaps);
     default:
       return cudaErrorInvalidValue;
   }

@@ -39,6 +39,17 @@ struct TcParams {
   // group_m row blocks; inside a band the row block varies fastest, then the
   // column tile, so one band's X rows stay in L2 while the band sweeps N.
   int group_m;
+  // K-split tail (CTA-pair kernel, static schedule): when ksplit >= 2 the
+  // leftover tiles are not cut along N but along K into ksplit parts, each on
+  // its own pair in the last wave.  Every part writes the accumulator columns
+  // it does not own to tail_ws, waits (bounded) until all parts of the tile
+  // have written, then sums the columns it owns over all parts in part order
+  // (deterministic) and runs the epilogue on them.  tail_cnt: zeroed device
+  // ints, two per (leftover tile, CTA of the pair, epilogue warp); the last
+  // part to finish sets them back to zero.
+  int ksplit;
+  float *tail_ws;
+  int *tail_cnt;
   // Column-parallel all-gather fused into the epilogue (CTA-pair kernel):
   // every Y chunk is also stored at the same offsets from y_peers[0..n_peers)
   // -- other GPUs' Y buffers mapped into this process -- so the shards
@@ -64,14 +75,22 @@ int tc_smem_bytes();
 // 2 x min(tiles, co-resident pairs, max_pairs if > 0).  tail_split: 0 =
 // choose, 1/2/4 = cut the leftover tiles into that many column parts.
 int tc2_smem_bytes();
+// tail_split: 0 = choose, 1/2/4 = cut the leftover tiles into that many
+// column parts, -s (2 <= s <= 8) = split them along K into s parts.
 // sched_counter: a zeroed device int for the dynamic scheduler, or nullptr
 // for the static round-robin schedule.
+// workspace / workspace_bytes: the call's workspace (layout in workspace.h,
+// counter regions zero) for the K-split tail, or nullptr; without room for
+// the chosen split's partial sums the tail is cut along N instead.
 // ym: TMA store maps of Y (nullptr: per-thread stores to p.y / p.y_peers).
 cudaError_t tc2_launch(int mode, const CUtensorMap &a, const CUtensorMap &b0, const CUtensorMap &b1,
-                       TcParams p, int max_pairs, int tail_split, int *sched_counter, cudaStream_t stream,
-                       const YStoreMaps *ym = nullptr);
+                       TcParams p, int max_pairs, int tail_split, int *sched_counter, void *workspace,
+                       size_t workspace_bytes, cudaStream_t stream, const YStoreMaps *ym = nullptr);
 // Device bytes the dynamic scheduler needs (one zeroed int).
 constexpr size_t kTc2SchedBytes = 256;
+// Workspace the K-split tail may need on a GPU with `sm_count` SMs: the
+// counter regions and the partial sums of at most one part per pair.
+size_t tc2_tail_workspace_bytes(int sm_count);
 int tc_threads();
 int tc_tile_n(int mode);
 cudaError_t tc_launch(int mode, const CUtensorMap &a, const CUtensorMap &b0, const CUtensorMap &b1,

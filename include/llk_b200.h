@@ -179,10 +179,10 @@ int llk_diag_timeout_probe(int device, int64_t limit_ns);
  * them would need device memory.  Limits: 1 <= M <= 128 (else
  * LLK_ERR_UNSUPPORTED) and N <= LLK_DECODE_NOALLOC_MAX_N (else
  * LLK_ERR_NOMEM: the array holds the counters of at most that many
- * columns).  The workspace a launch needs is 256 KB + 256 bytes of counters
- * plus, when CTAs share a column tile, 4096 * Mp bytes per CTA (Mp = M
- * rounded up to 16, 32, 64 or 128); when the default grid's share would not
- * fit, the call runs on fewer CTAs instead (possible only for M > 32).
+ * columns).  The workspace a launch needs is 264 KB (8 KB + 256 KB) of counters
+ * plus, when a stream-K grid has CTAs sharing a column tile, 4096 * Mp bytes
+ * per CTA (Mp = M rounded up to 16, 32, 64 or 128); when that would not fit,
+ * the call runs on fewer CTAs instead (possible only for M > 32).
  * Rows of X/Wg/Wu need 16-byte aligned starts and pitches, Y a start
  * aligned to its element size (else LLK_ERR_ALIGN).  Y is bf16, or f32
  * when gpu->y_dtype == LLK_DTYPE_FP32.
@@ -371,11 +371,14 @@ typedef struct llk_launch_plan {
   int block_n;   /* columns of Y per tile */
   int block_k;   /* K per pipeline stage */
   int stages;    /* shared-memory pipeline depth */
-  int split_k;   /* K partitions (decode) */
+  int split_k;   /* decode: K partitions; CTA-pair kernel: tail of leftover tiles, 0 = choose,
+                    1/2/4 = that many column parts, -s = s K parts (2 <= s <= 8) */
   int grid;      /* CTAs launched */
   int threads;   /* threads per CTA */
   int smem_bytes;
-  int sched;     /* CTA-pair kernel: 1 = static round-robin, 0 = dynamic work counter (built-in: from 12 waves of tiles) */
+  int sched;     /* CTA-pair kernel: 1 = static round-robin, 0 = dynamic work counter (built-in: from 12 waves of
+                    tiles).  Decode kernel: 1 = one cluster of split_k CTAs per 128-column tile, partial sums
+                    reduced in distributed shared memory (grid = tiles x split_k); 0 = stream-K over grid CTAs */
 } llk_launch_plan;
 
 uint64_t llk_kernel_key_hash(const llk_kernel_key *key);

@@ -66,10 +66,11 @@ def _rank_main(rank, world, port, q):
                 y = layer(xd)
             torch.cuda.synchronize()
             st = capi.lib().llk_synchronize(rank, None)
-            # the CTA-pair / one-CTA kernels accumulate each element in the
-            # same order whatever the column range; the decode kernel's
-            # split-K layout follows the shard width, so compare by value
-            same = bool(torch.equal(y, ref)) if M > 16 else float((y - ref).abs().max() / ref.abs().max()) < 1e-5
+            # a shard is a smaller problem than the whole: its tail may be
+            # split differently (decode split-K, CTA-pair K-split tail), so
+            # compare by value
+            d = float((y.float() - ref.float()).abs().max() / ref.float().abs().max())
+            same = d < (1e-5 if odt == "f32" else 1e-2)
             out.append((i, same, st))
             dist.barrier()
             layer.close()
