@@ -251,7 +251,7 @@ def reference_arm(args):
                                 f"about {mean * 1e3 * M / rows:.0f} ms per step at this rate",
             "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
             "data": "synthetic (seeded splitmix64/Box-Muller, X~N(0,1), W~N(0,0.02), bf16)",
-            "config": {"workload": "c3 llama7b-prefill swiglu", "M": M, "K": K, "N": N, "sample_rows": rows},
+            "config": {"workload": "c3 llama7b-prefill swiglu", "M": M, "K": K, "N": N, "math_mode": "strict", "sample_rows": rows},
             "cpu_baseline": {"value": value, "unit": UNIT, "cores": threads, "kind": "port", "sample": sample},
             "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
             "note": "the reference's own path (MLIR/LLVM ORC JIT) cannot be built here; its naive test oracle is "
@@ -773,6 +773,24 @@ def single_gpu_extras(args, dev, stream, peaks, headline_tflops):
     c = CONFIG
     g = torch.Generator(device=dev).manual_seed(3)
     X = (torch.randn((c["M"], c["K"]), generator=g, device=dev) * c["x_std"]).bfloat16()
+    # the headline's kernel with the fast epilogue (math_mode bounded_fast)
+    Wg = (torch.randn((c["K"], c["N"]), generator=g, device=dev) * c["w_std"]).bfloat16()
+    Wu = (torch.randn((c["K"], c["N"]), generator=g, device=dev) * c["w_std"]).bfloat16()
+    Y = torch.empty((c["M"], c["N"]), dtype=torch.bfloat16, device=dev)
+    fsets, _ = input_sets(dev, [X, Wg, Wu, Y], l2)
+
+    def fast(i):
+        a_, b_, c_, d_ = fsets[i % len(fsets)]
+        llk.fused_swiglu(a_, b_, c_, out=d_, math_mode="bounded_fast")
+
+    for i in range(3):
+        fast(i)
+    fms = time_back_to_back(fast, steps, stream) / steps
+    llk.synchronize(dev.index)
+    out["c3_bounded_fast"] = {"tflops": 4.0 * c["M"] * c["N"] * c["K"] / (fms * 1e-3) / 1e12, "ms": fms,
+                              "what": "config 3 with math_mode bounded_fast (__expf / __fdividef epilogue); the "
+                                      "headline runs the strict epilogue (expf, IEEE division)"}
+    del fsets, Wg, Wu, Y
     W = (torch.randn((c["K"], 2 * c["N"]), generator=g, device=dev) * c["w_std"]).bfloat16()
     cb3_ms = cublas_ms(X, W, None)
     cb3_tf = 4.0 * c["M"] * c["N"] * c["K"] / (cb3_ms * 1e-3) / 1e12
@@ -811,7 +829,27 @@ def sharded_extras(args, dev, stream, rank, world, peaks, barrier, max_over_rank
     out = {}
     l2 = torch.cuda.get_device_properties(dev).L2_cache_size
 
-    def run(cfg, steps, seed):
+    def graph_ms(fn, steps):
+        """Per-launch time of `steps` back-to-back launches replayed from
+        one CUDA graph (captured on a side stream, replayed on `stream`):
+        the launches without the host's per-call cost, as a decode loop
+        runs them."""
+        g = torch.cuda.CUDAGraph()
+        side = torch.cuda.Stream(dev)
+        side.wait_stream(stream)
+        with torch.cuda.stream(side):
+            with torch.cuda.graph(g, stream=side, capture_error_mode="thread_local"):
+                for i in range(steps):
+                    fn(i)
+        torch.cuda.synchronize()
+        g.replay()
+        torch.cuda.synchronize()
+        barrier()
+        ms = time_back_to_back(lambda i: g.replay(), 3, stream) / (3 * steps)
+        del g
+        return ms
+
+    def run(cfg, steps, seed, graph=False):
         c = dg.CONFIGS[cfg]
         M, K, N = c["M"], c["K"], c["N"]
         b, e = llk.shard_columns(N, world, rank)
@@ -830,25 +868,30 @@ def sharded_extras(args, dev, stream, rank, world, peaks, barrier, max_over_rank
         torch.cuda.synchronize()
         barrier()
         ms = max_over_ranks(time_back_to_back(fn, steps, stream)) / steps
+        gms = max_over_ranks(graph_ms(fn, steps)) if graph else None
         torch.cuda.synchronize()
         llk.synchronize(dev.index)
         rows, cols = parity_points(M, e - b, seed=seed + 17 * rank, n_random=1024)
         err = max_over_ranks(points_rel_err(xd, gd, ud, sets[0][3], rows, cols))
         del sets, xd, gd, ud, yd
         torch.cuda.empty_cache()
-        return M, K, N, e - b, ms, {"max_rel_err": err, "points_per_rank": int(rows.size)}
+        return M, K, N, e - b, ms, gms, {"max_rel_err": err, "points_per_rank": int(rows.size)}
 
     dec = {}
     for i, cfg in enumerate(("c4_m1", "c4_m4", "c4_m16")):
-        M, K, N, n_r, ms, par = run(cfg, max(5, min(args.steps, 200)), 41 + i)
+        M, K, N, n_r, ms_eager, ms, par = run(cfg, max(5, min(args.steps, 200)), 41 + i, graph=True)
         byts = 2 * M * K + 4 * K * N + 2 * M * N
         dec[cfg] = {"us": ms * 1e3, "GB/s": byts / (ms * 1e-3) / 1e9,
                     "frac_of_hbm_per_gpu": byts / (ms * 1e-3) / 1e9 / world / peaks["hbm"],
-                    "shard_cols_rank0": n_r, "tflops": 4.0 * M * N * K / (ms * 1e-3) / 1e12, "parity": par}
+                    "shard_cols_rank0": n_r, "tflops": 4.0 * M * N * K / (ms * 1e-3) / 1e12, "parity": par,
+                    "us_eager": ms_eager * 1e3,
+                    "timing": "us: back-to-back launches replayed from one CUDA graph (inputs rotating over sets "
+                              "> 2x L2), max over ranks; us_eager: the same launches issued one by one from Python "
+                              "(includes the host's ~15-20 us per call)"}
     out["decode_c4"] = dec
     # config 5 after the decode shapes: its seconds at the power cap lower the
     # SM clock for a few seconds afterwards, which slows the decode kernel.
-    M, K, N, n_r, ms, par = run("c5", max(5, min(args.steps, 40)), 55)
+    M, K, N, n_r, ms, _, par = run("c5", max(5, min(args.steps, 40)), 55)
     tf = 4.0 * M * N * K / (ms * 1e-3) / 1e12
     out["swiglu_c5"] = {"workload": "c5 llama70b-prefill swiglu X[8192,8192] W[8192,28672] bf16",
                         "tflops": tf, "ms": ms, "frac_of_sustained_per_gpu": tf / world / peaks["sustained"],

@@ -36,6 +36,12 @@ LLK_DTYPE_BF16 = 0
 LLK_DTYPE_FP16 = 1
 LLK_DTYPE_FP32 = 2
 
+# enum llk_math_mode (KernelKey.h MathMode; the op's math_mode attribute)
+LLK_MATH_STRICT = 0
+LLK_MATH_BOUNDED_FAST = 1
+LLK_MATH_UNSAFE_FAST = 2
+MATH_MODES = {"strict": LLK_MATH_STRICT, "bounded_fast": LLK_MATH_BOUNDED_FAST, "unsafe_fast": LLK_MATH_UNSAFE_FAST}
+
 # enum llk_variant
 VARIANTS = {"auto": 0, "tc": 1, "decode": 2, "simt": 3}
 
@@ -64,7 +70,7 @@ class KernelContext(ctypes.Structure):
 
 class GpuContext(ctypes.Structure):
     _fields_ = [("device", ctypes.c_int), ("stream", ctypes.c_void_p), ("y_dtype", ctypes.c_int),
-                ("variant", ctypes.c_int), ("reserved", ctypes.c_int * 4)]
+                ("variant", ctypes.c_int), ("math_mode", ctypes.c_int), ("reserved", ctypes.c_int * 3)]
 
 
 class CudaTarget(ctypes.Structure):

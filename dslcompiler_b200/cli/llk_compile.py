@@ -5,8 +5,11 @@ positional input .mlir and ``--M/--N/--K`` for dynamic dimensions; prints
 "Compilation successful" and exits 0, or reports "Failed to parse <file>" /
 "Compilation pipeline failed" and exits 1.  Instead of JIT-compiling CPU code
 it verifies the op, lowers it to the micro.kernel that dispatches to the
-sm_100a kernel (``--emit=micro`` prints it) and resolves the launch plan (the
-"object code" of this backend).
+sm_100a kernel (``--emit=micro`` prints it; ``dslcompiler_b200.micro.run_micro``
+runs it) and resolves the launch plan (the "object code" of this backend).
+``--emit=micro-search-space`` prints the ``micro.search_space`` of legal
+launch-plan choices for each op instead (the spec's
+``--llk-to-micro-search-space``), which ``llk-tune --search-space`` reads.
 """
 from __future__ import annotations
 
@@ -14,7 +17,7 @@ import argparse
 import json
 import sys
 
-from .. import compiler, schedule
+from .. import compiler, micro, schedule
 
 
 def main(argv=None) -> int:
@@ -23,7 +26,7 @@ def main(argv=None) -> int:
     ap.add_argument("--M", type=int, default=0)
     ap.add_argument("--N", type=int, default=0)
     ap.add_argument("--K", type=int, default=0)
-    ap.add_argument("--emit", choices=["none", "micro", "plan"], default="none")
+    ap.add_argument("--emit", choices=["none", "micro", "plan", "micro-search-space"], default="none")
     ap.add_argument("--variant", choices=["auto", "tc", "decode"], default="auto")
     ap.add_argument("--schedule-db", default=None, help="install B200 schedules from this DB first")
     ap.add_argument("-o", "--output", default=None, help="write the emitted text here")
@@ -44,6 +47,9 @@ def main(argv=None) -> int:
         for op in ops:
             compiler.verify(op)
             M, N, K = compiler.resolve_shape(op, a.M, a.N, a.K)
+            if a.emit == "micro-search-space":
+                out.append(micro.emit_search_space(micro.search_space(op.op, M, N, K)))
+                continue
             low = compiler.lower_to_micro(op, M, N, K, a.variant)
             if a.emit == "micro":
                 out.append(low.text)

@@ -6,10 +6,12 @@ reference writes its candidates unmeasured (llk-tune.cpp:226-232), this one
 measures every sm_100a candidate on the GPU (CUDA events, L2 evicted before
 each launch, median of --iters) and records measured_gflops.
 
-Candidates (launch plans the kernels accept):
-  * tcgen05 kernel: CTA pairs or single CTAs (block_m 256 / 128), tail split
-    1 / 2 / 4 / auto for pairs, persistent grid sizes;
-  * decode kernel (SwiGLU, M <= 128): grid sizes x pipeline stages.
+Candidates: the legal launch plans of the op's ``micro.search_space``
+(``dslcompiler_b200.micro``: CTA pairs or single CTAs, the tail split of
+the leftover tiles along N or K, static or dynamic schedule, persistent grid
+sizes; for small-M SwiGLU the decode kernel's stages, grid and cluster
+split), or of a stored space given with ``--search-space FILE`` (the output
+of ``llk-compile --emit micro-search-space``).
 --install merges the results into a schedule DB file.
 """
 from __future__ import annotations
@@ -18,22 +20,7 @@ import argparse
 import statistics
 import sys
 
-from .. import schedule
-
-
-def candidates(op: str, M: int, N: int, K: int, base_tc: dict, base_dec: dict | None) -> list[dict]:
-    out = []
-    if M > 128:
-        for split in (0, 1, 2, 4):
-            for grid in (148, 144, 128):
-                out.append(dict(base_tc, block_m=256, stages=6, split_k=split, grid=grid))
-    for grid in (148, 132):
-        out.append(dict(base_tc, block_m=128, stages=4, split_k=1, grid=grid))
-    if base_dec is not None:
-        for grid in (74, 112, 148, 222, 296):
-            for stages in (3, 4, 6, 8):
-                out.append(dict(base_dec, grid=grid, stages=stages))
-    return out
+from .. import micro, schedule
 
 
 def main(argv=None) -> int:
@@ -46,6 +33,7 @@ def main(argv=None) -> int:
     ap.add_argument("--op", choices=["swiglu", "matmul"], default="swiglu")
     ap.add_argument("--iters", type=int, default=20)
     ap.add_argument("--install", default=None, help="merge the top entries into this schedule DB")
+    ap.add_argument("--search-space", default=None, help="micro.search_space file to draw the candidates from")
     a = ap.parse_args(argv)
     M, N, K = a.M, a.N, a.K
     from .. import capi
@@ -60,7 +48,17 @@ def main(argv=None) -> int:
                         thread_count=capi.VARIANTS["decode"]) if (a.op == "swiglu" and M <= 128) else None
     base_tc = key_tc.plan(M)
     base_dec = key_dec.plan(M) if key_dec else None
-    cands = candidates(a.op, M, N, K, base_tc, base_dec)
+    if a.search_space:
+        space = micro.parse_search_space(open(a.search_space).read())
+        if (space.M, space.N, space.K) != (M, N, K) or space.workload != opname:
+            print(f"error: {a.search_space} is the space of {space.workload} M={space.M} N={space.N} K={space.K}",
+                  file=sys.stderr)
+            return 1
+    else:
+        space = micro.search_space(opname, M, N, K)
+    cands = micro.candidates(space)
+    if key_dec is None:
+        cands = [c for c in cands if c["variant"] != capi.VARIANTS["decode"]]
     print(f"M={M} (bucket {bucket}) N={N} K={K}")
     print(f"Generated {len(cands)} candidate configs (sm_100a launch plans)")
     results = []

@@ -26,10 +26,8 @@ from . import capi
 
 DYN = -1  # '?' dimension
 
-_OP_RE = re.compile(
-    r"(?P<res>%[\w.]+)\s*=\s*llk\.(?P<op>fused_swiglu|matmul)\s+ins\((?P<ins>[^)]*)\)\s*"
-    r"outs\((?P<outs>[^)]*)\)\s*(?P<attrs>\{.*?\})?\s*->\s*(?P<rtype>tensor<[^>]*>)", re.S)
 _TENSOR_RE = re.compile(r"tensor<([^>]*)>")
+_OP_NAME_RE = re.compile(r'(?P<res>%[\w.#]+(?::\d+)?)\s*=\s*(?P<q>"?)llk\.(?P<op>fused_swiglu|matmul)(?P=q)')
 
 
 class VerifyError(ValueError):
@@ -67,21 +65,102 @@ class LLKOp:
         return self.types[0]
 
 
+def _balanced_end(text: str, start: int, open_ch: str, close_ch: str) -> int:
+    depth = 0
+    for i in range(start, len(text)):
+        if text[i] == open_ch:
+            depth += 1
+        elif text[i] == close_ch:
+            depth -= 1
+            if depth == 0:
+                return i + 1
+    raise VerifyError(f"unbalanced {open_ch}{close_ch}")
+
+
+def _types(text: str) -> list:
+    return [TensorType.parse("tensor<" + t) for t in text.split("tensor<")[1:]]
+
+
+def _attrs(body: str) -> dict:
+    from .micro import parse_attr_dict
+
+    return {k: str(v) for k, v in parse_attr_dict(body).items()}
+
+
 def parse_llk(text: str) -> list[LLKOp]:
-    """Every llk.fused_swiglu / llk.matmul op in an MLIR text."""
+    """Every llk.fused_swiglu / llk.matmul op in an MLIR text, in the ops'
+    custom assembly format (``include/LLK/Dialect/LLKOps.td:43-48``:
+    ``%r = llk.op ins(%a, .. : T, ..) outs(%i : T) {attrs} -> T``) or the
+    generic one (``%r = "llk.op"(%a, .., %i) {attrs} : (T, ..) -> T``), with
+    any line breaks, spacing and comments."""
+    text = re.sub(r"//[^\n]*", "", text)
     ops = []
-    for m in _OP_RE.finditer(text):
-        ins, outs = m.group("ins"), m.group("outs")
-        in_names, in_types = [s.strip() for s in ins.split(":")[0].split(",")], ins.split(":", 1)[1]
-        out_names, out_types = [s.strip() for s in outs.split(":")[0].split(",")], outs.split(":", 1)[1]
-        types = [TensorType.parse("tensor<" + t) for t in in_types.split("tensor<")[1:]]
-        types += [TensorType.parse("tensor<" + t) for t in out_types.split("tensor<")[1:]]
+    for m in _OP_NAME_RE.finditer(text):
+        i = m.end()
+        if m.group("q"):  # generic form
+            j = text.index("(", i)
+            k = _balanced_end(text, j, "(", ")")
+            names = [s.strip() for s in text[j + 1:k - 1].split(",") if s.strip()]
+            rest = text[k:]
+            attrs = {}
+            am = re.match(r"\s*\{", rest)
+            if am:
+                a0 = k + am.end() - 1
+                a1 = _balanced_end(text, a0, "{", "}")
+                attrs = _attrs(text[a0:a1])
+                k = a1
+            tm = re.match(r"\s*:\s*\(", text[k:])
+            if not tm:
+                raise VerifyError("generic llk op without a function type")
+            t0 = k + tm.end() - 1
+            t1 = _balanced_end(text, t0, "(", ")")
+            types = _types(text[t0:t1])
+            rm = re.match(r"\s*->\s*(tensor<[^>]*>)", text[t1:])
+            if not rm:
+                raise VerifyError("generic llk op without a result type")
+            ops.append(LLKOp(m.group("op"), names, types, TensorType.parse(rm.group(1)), attrs))
+            continue
+        # custom form
+        im = re.match(r"\s*ins\s*\(", text[i:])
+        if not im:
+            continue
+        j = i + im.end() - 1
+        k = _balanced_end(text, j, "(", ")")
+        ins = text[j + 1:k - 1]
+        om = re.match(r"\s*outs\s*\(", text[k:])
+        if not om:
+            raise VerifyError(f"llk.{m.group('op')} without outs(...)")
+        j2 = k + om.end() - 1
+        k2 = _balanced_end(text, j2, "(", ")")
+        outs = text[j2 + 1:k2 - 1]
         attrs = {}
-        if m.group("attrs"):
-            for kv in re.finditer(r"(\w+)\s*=\s*([^,}]+(?:<[^>]*>)?)", m.group("attrs")):
-                attrs[kv.group(1)] = kv.group(2).strip()
-        ops.append(LLKOp(m.group("op"), in_names + out_names, types, TensorType.parse(m.group("rtype")), attrs))
+        am = re.match(r"\s*(attributes\s*)?\{", text[k2:])
+        pos = k2
+        if am:
+            a0 = k2 + am.end() - 1
+            a1 = _balanced_end(text, a0, "{", "}")
+            attrs = _attrs(text[a0:a1])
+            pos = a1
+        rm = re.match(r"\s*->\s*(tensor<[^>]*>)", text[pos:])
+        if not rm:
+            raise VerifyError(f"llk.{m.group('op')} without a result type")
+        in_names, in_types = ins.split(":", 1)
+        out_names, out_types = outs.split(":", 1)
+        names = [s.strip() for s in in_names.split(",")] + [s.strip() for s in out_names.split(",")]
+        ops.append(LLKOp(m.group("op"), names, _types(in_types) + _types(out_types),
+                         TensorType.parse(rm.group(1)), attrs))
     return ops
+
+
+def op_math_mode(op: LLKOp) -> str:
+    """The op's math_mode attribute (#llk.math_mode<strict> ..) as a name;
+    strict when absent (the fused lowering's epilogue)."""
+    v = op.attrs.get("math_mode", "")
+    m = re.search(r"<\s*(\w+)\s*>", v)
+    name = m.group(1) if m else (v.strip('"') or "strict")
+    if name not in capi.MATH_MODES:
+        raise VerifyError(f"unknown math_mode {name!r}")
+    return name
 
 
 def verify(op: LLKOp) -> None:
@@ -150,7 +229,7 @@ class Lowered:
     y_dtype: str
 
 
-def _plan(op: str, M: int, N: int, K: int, y_dtype: str, variant: str = "auto") -> dict:
+def _plan(op: str, M: int, N: int, K: int, y_dtype: str, variant: str = "auto", math_mode: str = "strict") -> dict:
     from .swiglu import KernelKey
 
     opcode = capi.LLK_OP_FUSED_SWIGLU if op == "fused_swiglu" else capi.LLK_OP_MATMUL
@@ -158,9 +237,17 @@ def _plan(op: str, M: int, N: int, K: int, y_dtype: str, variant: str = "auto") 
     if variant == "auto":
         # the dispatcher's rule: decode kernel for <= 16 tokens of SwiGLU
         variant = "decode" if (op == "fused_swiglu" and M <= 16) else "tc"
+    math = capi.MATH_MODES[math_mode] if op == "fused_swiglu" else capi.LLK_MATH_STRICT
     key = KernelKey(operation=opcode, output_type=out, M_bucket=capi.lib().llk_classify_m(M), N=N, K=K,
-                    thread_count=capi.VARIANTS[variant])
+                    thread_count=capi.VARIANTS[variant], math_mode=math)
     return key.plan(M)
+
+
+def _plan_attrs(plan: dict) -> str:
+    """The launch-plan fields a micro.kernel carries (read back by
+    micro.parse_micro_kernel to dispatch it)."""
+    return (f"grid = {plan['grid']}, split_k = {plan['split_k']}, sched = {plan['sched']}, "
+            f"threads = {plan['threads']}, smem_bytes = {plan['smem_bytes']}")
 
 
 _DEF_RE = re.compile(r"^\s*(%\w+)(?:\s*,\s*%\w+)?\s*=\s*micro\.(\w+)\b(.*)$")
@@ -234,7 +321,8 @@ def verify_micro(text: str) -> list[str]:
 def lower_to_micro(op: LLKOp, M: int, N: int, K: int, variant: str = "auto", schedule_id: str = "") -> Lowered:
     """The micro.kernel for the kernel and plan that will run this op."""
     y_dtype = op.result_type.dtype if op.result_type.dtype in ("bf16", "f32") else "bf16"
-    plan = _plan(op.op, M, N, K, y_dtype, variant)
+    math_mode = op_math_mode(op) if op.op == "fused_swiglu" else "strict"
+    plan = _plan(op.op, M, N, K, y_dtype, variant, math_mode)
     v = plan["variant"]
     swiglu = op.op == "fused_swiglu"
     name = f"{op.op}_M{M}_N{N}_K{K}"
@@ -248,7 +336,7 @@ def lower_to_micro(op: LLKOp, M: int, N: int, K: int, variant: str = "auto", sch
         mma_n = 2 * bn if swiglu else bn
         engine = "tcgen05.cta_group::2" if pair else "tcgen05.cta_group::1"
         L.append(f'micro.kernel @{name} attributes {{workload = "{op.op}", target = "b200-sm100a", '
-                 f'candidate = "{cand}", schedule_id = "{sid}", grid = {plan["grid"]}}} {{')
+                 f'candidate = "{cand}", schedule_id = "{sid}", {_plan_attrs(plan)}}} {{')
         L.append(f"  micro.spatial_for %bm = 0 to {M} step {bm} map = #micro.map<{owner}> {{")
         L.append(f"    micro.spatial_for %bn = 0 to {N} step {bn} map = #micro.map<{owner}> {{")
         L.append(f"      %acc = micro.alloc tensor<{bm}x{mma_n}xf32> memory = #micro.memory<acc>")
@@ -273,7 +361,7 @@ def lower_to_micro(op: LLKOp, M: int, N: int, K: int, variant: str = "auto", sch
         if swiglu:
             L.append(f"      %gate = micro.slice %acc {{offsets = [0, 0], shape = [{bm}, {bn}]}}")
             L.append(f"      %up = micro.slice %acc {{offsets = [0, {bn}], shape = [{bm}, {bn}]}}")
-            L.append('      %silu = micro.vector "silu" %gate {math_mode = "strict"}')
+            L.append(f'      %silu = micro.vector "silu" %gate {{math_mode = "{math_mode}"}}')
             L.append('      %out = micro.vector "mul" %silu, %up')
             L.append(f"      micro.store %out, %arg3 {{src_memory = #micro.memory<acc>, dst_memory = #micro.memory<dram>}} : tensor<{bm}x{bn}x{y_dtype}>")
         else:
@@ -287,7 +375,7 @@ def lower_to_micro(op: LLKOp, M: int, N: int, K: int, variant: str = "auto", sch
         # two accumulators (adjacent TMEM columns on the device).
         mp, bk = plan["block_m"], plan["block_k"]
         L.append(f'micro.kernel @{name} attributes {{workload = "{op.op}", target = "b200-sm100a", '
-                 f'candidate = "decode_kernel", schedule_id = "{sid}", grid = {plan["grid"]}}} {{')
+                 f'candidate = "decode_kernel", schedule_id = "{sid}", M = {M}, {_plan_attrs(plan)}}} {{')
         L.append(f"  micro.spatial_for %bn = 0 to {N} step 128 map = #micro.map<worker> {{")
         for w in ["wg", "wu"]:
             L.append(f"    %acc_{w} = micro.alloc tensor<128x{mp}xf32> memory = #micro.memory<acc>")
@@ -304,7 +392,7 @@ def lower_to_micro(op: LLKOp, M: int, N: int, K: int, variant: str = "auto", sch
                      f"accumulator = #micro.dtype<f32>, engine = \"tcgen05.cta_group::1\", owner = #micro.owner<matrix_engine>}}")
         L.append("      }")
         L.append("    }")
-        L.append('    %silu = micro.vector "silu" %acc_wg {math_mode = "strict"}')
+        L.append(f'    %silu = micro.vector "silu" %acc_wg {{math_mode = "{math_mode}"}}')
         L.append('    %out = micro.vector "mul" %silu, %acc_wu')
         L.append(f"    micro.store %out, %arg3 {{src_memory = #micro.memory<acc>, dst_memory = #micro.memory<dram>}} : tensor<{mp}x128x{y_dtype}>")
         L.append("  }")

@@ -37,9 +37,10 @@ size_t decode_counter_bytes(int64_t N);
 bool decode_plan_valid(int64_t M, int64_t N, int64_t K, const DecodePlan &d);
 // wg, wu: weight tensor maps with a 64-column x 64-k box (2-D over
 // row-major [K, N], or 3-D over slab-major packed weights when slab_major);
-// x: token tensor map, box {64 k, d.block_m rows}.
+// x: token tensor map, box {64 k, d.block_m rows}.  fast_math: the fast
+// SwiGLU epilogue instead of the strict one (separate kernel instantiations).
 cudaError_t decode_launch(const CUtensorMap &wg, const CUtensorMap &wu, const CUtensorMap &x, void *y, int64_t ldy,
                           int y_f32, int64_t M, int64_t N, int64_t K, void *workspace, int *status,
-                          const DecodePlan &d, int slab_major, cudaStream_t stream);
+                          const DecodePlan &d, int slab_major, int fast_math, cudaStream_t stream);
 
 }  // namespace llk_b200

@@ -235,6 +235,15 @@ llk_kernel_key make_key(int op, int out_dtype, int64_t M, int64_t N, int64_t K, 
 // Kernel family for a request: the decode kernel for small M when its
 // shape rules hold, the tcgen05 kernel otherwise; SIMT when TMA cannot
 // describe the operands.
+// A call's kernel request: the variant (enum llk_variant) in the low byte,
+// the math mode (enum llk_math_mode) in the next, as carried from the
+// llk_gpu_context through the staging and pipelining helpers.
+int pack_request(const llk_gpu_context *gpu) {
+  return gpu ? ((gpu->variant & 0xff) | ((gpu->math_mode & 0xff) << 8)) : LLK_VARIANT_AUTO;
+}
+int request_variant(int request) { return request & 0xff; }
+int request_math_mode(int request) { return (request >> 8) & 0xff; }
+
 int choose_variant(int requested, bool tma_ok, bool decode_ok, int64_t M, int64_t K) {
   if (requested == LLK_VARIANT_SIMT) return LLK_VARIANT_SIMT;
   if (!tma_ok || K == 0) return requested == LLK_VARIANT_AUTO ? LLK_VARIANT_SIMT : -1;
@@ -359,11 +368,14 @@ int launch_device(DeviceState &ds, int op, const DevTensor &x, const DevTensor &
   const bool tma_ok = x.inner == 1 && y.inner == 1 && aligned16(x.data) && (x.ld * 2) % 16 == 0 && x.ld >= K &&
                       weight_ok(wg) && (!swiglu || weight_ok(wu));
   const bool decode_ok = swiglu && tma_ok && decode_supported(M, N, K, y_f32);
-  const int variant = choose_variant(requested, tma_ok, decode_ok, M, K);
+  const int variant = choose_variant(request_variant(requested), tma_ok, decode_ok, M, K);
+  const int math_mode = request_math_mode(requested);
+  const bool fast_math = math_mode != LLK_MATH_STRICT;
   if (variant < 0) return LLK_ERR_UNSUPPORTED;
 
   llk_kernel_key key = make_key(op, y_f32 ? LLK_DTYPE_FP32 : LLK_DTYPE_BF16, M, N, K, variant);
   key.weight_layout = slab ? 1 : 0;  // Layout::PackedKN analogue
+  key.math_mode = static_cast<uint8_t>(swiglu ? math_mode : LLK_MATH_STRICT);  // matmul has no epilogue math
   llk_launch_plan plan = plan_for(key, M, ds.sm_count);
   cudaError_t e = cudaSuccess;
 
@@ -371,7 +383,7 @@ int launch_device(DeviceState &ds, int op, const DevTensor &x, const DevTensor &
     int mode = swiglu ? 0 : (accumulate ? 2 : 1);
     e = simt_launch(mode, x.data, x.ld, x.inner, wg.data, swiglu ? wu.data : wg.data, wg.ld, wg.inner,
                     swiglu ? wu.ld : wg.ld, swiglu ? wu.inner : wg.inner, const_cast<void *>(y.data), y.ld, y.inner,
-                    y_f32, M, N, K, slab ? 1 : 0, stream);
+                    y_f32, M, N, K, slab ? 1 : 0, fast_math ? 1 : 0, stream);
     return e == cudaSuccess ? LLK_OK : LLK_ERR_CUDA;
   }
 
@@ -398,7 +410,7 @@ int launch_device(DeviceState &ds, int op, const DevTensor &x, const DevTensor &
     if ((rc = encode_weight_tmap(&tu, wu)) != LLK_OK) return rc;
     if ((rc = encode_tmap(&tx, x.data, K, M, x.ld * 2, 64, d.block_m)) != LLK_OK) return rc;
     e = decode_launch(tg, tu, tx, const_cast<void *>(y.data), y.ld, y_f32, M, N, K, ws, ds.status, d, slab ? 1 : 0,
-                      stream);
+                      fast_math ? 1 : 0, stream);
     return e == cudaSuccess ? LLK_OK : LLK_ERR_CUDA;
   }
 
@@ -412,7 +424,8 @@ int launch_device(DeviceState &ds, int op, const DevTensor &x, const DevTensor &
   } else {
     tb1 = tb0;
   }
-  const int mode = swiglu ? (y_f32 ? TC_SWIGLU_F32 : TC_SWIGLU_BF16) : (accumulate ? TC_MATMUL_F32_ACC : TC_MATMUL_F32);
+  const int mode = swiglu ? ((y_f32 ? TC_SWIGLU_F32 : TC_SWIGLU_BF16) | (fast_math ? TC_FAST_MATH : 0))
+                          : (accumulate ? TC_MATMUL_F32_ACC : TC_MATMUL_F32);
   const int tile_n = tc_tile_n(mode);
   const int ysz = y_f32 ? 4 : 2;
   TcParams p;
@@ -688,12 +701,13 @@ int run_op(int op, const Tensor2D *x, const Tensor2D *wg, const Tensor2D *wu, Te
            const DevTensor *packed_u = nullptr) {
   if (gpu && (gpu->y_dtype != LLK_DTYPE_BF16 && gpu->y_dtype != LLK_DTYPE_FP32)) return LLK_ERR_ARG;
   if (gpu && (gpu->variant < LLK_VARIANT_AUTO || gpu->variant > LLK_VARIANT_SIMT)) return LLK_ERR_ARG;
+  if (gpu && (gpu->math_mode < LLK_MATH_STRICT || gpu->math_mode > LLK_MATH_UNSAFE_FAST)) return LLK_ERR_ARG;
   int dev, rc;
   if ((rc = resolve_device(gpu, &dev)) != LLK_OK) return rc;
   DeviceState *ds;
   if ((rc = device_init(dev, &ds)) != LLK_OK) return rc;
   cudaStream_t stream = gpu ? static_cast<cudaStream_t>(gpu->stream) : nullptr;
-  const int requested = gpu ? gpu->variant : LLK_VARIANT_AUTO;
+  const int requested = pack_request(gpu);
   const int yel = y_f32 ? 4 : 2;
 
   Staged sx, sg, su, sy;
@@ -1436,7 +1450,7 @@ int llk_swiglu_column_parallel(const Tensor2D *x, const Tensor2D *wg_shard, cons
   if (gpu && gpu->device >= 0 && gpu->device != g->device) return LLK_ERR_ARG;
   const int y_f32 = (gpu && gpu->y_dtype == LLK_DTYPE_FP32) ? 1 : 0;
   if (gpu && gpu->y_dtype != LLK_DTYPE_BF16 && gpu->y_dtype != LLK_DTYPE_FP32) return LLK_ERR_ARG;
-  const int requested = gpu ? gpu->variant : LLK_VARIANT_AUTO;
+  const int requested = pack_request(gpu);
   const int64_t M = x->dim0, K = x->dim1;
   int64_t b, e;
   if (llk_shard_columns(N, g->n, g->rank, &b, &e) != LLK_OK) return LLK_ERR_ARG;

@@ -237,6 +237,26 @@ __device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
 // B200: 24 us against 22 us per tile at K = 4096; 5 us with __fdividef).
 __device__ __forceinline__ float silu_mul(float g, float u) { return __fdividef(g, 1.0f + __expf(-g)) * u; }
 
+// The strict epilogue of the fused lowering (the reference's math.exp /
+// arith.divf sequence, lib/Transforms/FuseDoubleContraction.cpp:189-196):
+// sigmoid = 1 / (1 + exp(-g)) with CUDA's accurate expf and the IEEE-rounded
+// division, silu = g * sigmoid, r = silu * u -- the same operations in the
+// same order.
+__device__ __forceinline__ float silu_mul_strict(float g, float u) {
+  const float sigmoid = 1.0f / (1.0f + expf(-g));
+  return (g * sigmoid) * u;
+}
+
+// Epilogue by math mode: kFast = bounded/unsafe fast (silu_mul), else strict.
+template <bool kFast>
+__device__ __forceinline__ float silu_mul_mode(float g, float u) {
+  if constexpr (kFast) {
+    return silu_mul(g, u);
+  } else {
+    return silu_mul_strict(g, u);
+  }
+}
+
 // ----------------------------------------------------- CTA pairs (2-SM MMA)
 __device__ __forceinline__ uint32_t cluster_ctarank() {
   uint32_t r;

@@ -109,7 +109,7 @@ __device__ __forceinline__ void store_y(const DecodeParams &p, int m, int n, flo
 // c_first .. c_last in batches of B whose loads are issued together, added
 // in CTA order.  Adding the zeros of a batch's unused entries leaves every
 // sum unchanged, so the order and result are those of a plain loop.
-template <int R, int B>
+template <bool kFast, int R, int B>
 __device__ __forceinline__ void fixup_tile(const DecodeParams &p, long long t, long long c_first, long long c_last,
                                            long long G, int r, int n, size_t slot_floats) {
   for (int m0 = 0; m0 < p.M; m0 += R) {
@@ -144,7 +144,7 @@ __device__ __forceinline__ void fixup_tile(const DecodeParams &p, long long t, l
     if (n < p.N) {
 #pragma unroll
       for (int j = 0; j < R; ++j)
-        if (j < rows) store_y(p, m0 + j, n, silu_mul(gs[j], us[j]));
+        if (j < rows) store_y(p, m0 + j, n, silu_mul_mode<kFast>(gs[j], us[j]));
     }
   }
 }
@@ -159,6 +159,7 @@ __device__ unsigned long long g_decode_trace[4096][8];
   } while (0)
 #endif
 
+template <bool kFast>
 __global__ void __launch_bounds__(kThreads, 1)
     decode_kernel(const __grid_constant__ CUtensorMap tm_wg, const __grid_constant__ CUtensorMap tm_wu,
                   const __grid_constant__ CUtensorMap tm_x, const DecodeParams p) {
@@ -348,7 +349,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           if (n < p.N) {
 #pragma unroll
             for (int j = 0; j < 16; ++j)
-              if (m0 + j < p.M) store_y(p, m0 + j, n, silu_mul(__uint_as_float(g[j]), __uint_as_float(uu[j])));
+              if (m0 + j < p.M) store_y(p, m0 + j, n, silu_mul_mode<kFast>(__uint_as_float(g[j]), __uint_as_float(uu[j])));
           }
         }
         tc_fence_before();
@@ -387,9 +388,9 @@ __global__ void __launch_bounds__(kThreads, 1)
         // 64 loads in flight: 4 token rows x 8 contributors at a time for
         // M <= 4, 16 rows x 2 contributors above.
         if (p.M <= 4)
-          fixup_tile<4, 8>(p, t, c_first, c_last, G, r, n, slot_floats);
+          fixup_tile<kFast, 4, 8>(p, t, c_first, c_last, G, r, n, slot_floats);
         else
-          fixup_tile<16, 2>(p, t, c_first, c_last, G, r, n, slot_floats);
+          fixup_tile<kFast, 16, 2>(p, t, c_first, c_last, G, r, n, slot_floats);
         if (etid == 0) p.counters[t] = 0;
       }
     }
@@ -435,10 +436,10 @@ __global__ void __launch_bounds__(kThreads, 1)
           us.w += uv[j].w;
         }
         const int n = t * kTileN + c;
-        if (n < p.N) store_y(p, m, n, silu_mul(gs.x, us.x));
-        if (n + 1 < p.N) store_y(p, m, n + 1, silu_mul(gs.y, us.y));
-        if (n + 2 < p.N) store_y(p, m, n + 2, silu_mul(gs.z, us.z));
-        if (n + 3 < p.N) store_y(p, m, n + 3, silu_mul(gs.w, us.w));
+        if (n < p.N) store_y(p, m, n, silu_mul_mode<kFast>(gs.x, us.x));
+        if (n + 1 < p.N) store_y(p, m, n + 1, silu_mul_mode<kFast>(gs.y, us.y));
+        if (n + 2 < p.N) store_y(p, m, n + 2, silu_mul_mode<kFast>(gs.z, us.z));
+        if (n + 3 < p.N) store_y(p, m, n + 3, silu_mul_mode<kFast>(gs.w, us.w));
       }
     }
     cluster_sync_all();
@@ -489,7 +490,8 @@ int max_active_clusters(int s, int smem) {
     if (it != cache.end()) return it->second;
   }
   int n = 0;
-  if (cudaFuncSetAttribute(decode_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024) == cudaSuccess) {
+  if (cudaFuncSetAttribute(decode_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024) ==
+      cudaSuccess) {
     cudaLaunchConfig_t cfg = {};
     cudaLaunchAttribute attr[1];
     attr[0].id = cudaLaunchAttributeClusterDimension;
@@ -501,7 +503,7 @@ int max_active_clusters(int s, int smem) {
     cfg.dynamicSmemBytes = smem;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    if (cudaOccupancyMaxActiveClusters(&n, decode_kernel, &cfg) != cudaSuccess) n = 0;
+    if (cudaOccupancyMaxActiveClusters(&n, decode_kernel<false>, &cfg) != cudaSuccess) n = 0;
   }
   cudaGetLastError();
   std::lock_guard<std::mutex> lk(mu);
@@ -603,7 +605,7 @@ bool decode_plan_valid(int64_t M, int64_t N, int64_t K, const DecodePlan &d) {
 
 cudaError_t decode_launch(const CUtensorMap &wg, const CUtensorMap &wu, const CUtensorMap &x, void *y, int64_t ldy,
                           int y_f32, int64_t M, int64_t N, int64_t K, void *workspace, int *status,
-                          const DecodePlan &d, int slab_major, cudaStream_t stream) {
+                          const DecodePlan &d, int slab_major, int fast_math, cudaStream_t stream) {
   if (!decode_plan_valid(M, N, K, d)) return cudaErrorInvalidValue;
   DecodeParams p;
   p.M = static_cast<int>(M);
@@ -629,7 +631,9 @@ cudaError_t decode_launch(const CUtensorMap &wg, const CUtensorMap &wu, const CU
   cudaGetDevice(&dev);
   const uint64_t bit = 1ull << (dev & 63);
   if (!(attr_set.load(std::memory_order_relaxed) & bit)) {
-    cudaError_t e = cudaFuncSetAttribute(decode_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
+    cudaError_t e = cudaFuncSetAttribute(decode_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
+    if (e != cudaSuccess) return e;
+    e = cudaFuncSetAttribute(decode_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
     if (e != cudaSuccess) return e;
     attr_set.fetch_or(bit);
   }
@@ -651,7 +655,8 @@ cudaError_t decode_launch(const CUtensorMap &wg, const CUtensorMap &wu, const CU
   cfg.stream = stream;
   cfg.attrs = attr;
   cfg.numAttrs = d.cluster >= 2 ? 2 : 1;
-  cudaError_t e = cudaLaunchKernelEx(&cfg, decode_kernel, wg, wu, x, p);
+  cudaError_t e = fast_math ? cudaLaunchKernelEx(&cfg, decode_kernel<true>, wg, wu, x, p)
+                            : cudaLaunchKernelEx(&cfg, decode_kernel<false>, wg, wu, x, p);
   if (e != cudaSuccess) return e;
   return cudaGetLastError();
 }

@@ -136,6 +136,7 @@ extern "C" int llk_swiglu_decode_noalloc(const Tensor2D *x, const Tensor2D *wg, 
   const int y_dtype = gpu ? gpu->y_dtype : LLK_DTYPE_BF16;
   if (y_dtype != LLK_DTYPE_BF16 && y_dtype != LLK_DTYPE_FP32) return LLK_ERR_ARG;
   const int y_f32 = y_dtype == LLK_DTYPE_FP32 ? 1 : 0;
+  if (gpu && (gpu->math_mode < LLK_MATH_STRICT || gpu->math_mode > LLK_MATH_UNSAFE_FAST)) return LLK_ERR_ARG;
 
   // The array's fixed size is the limit: the per-tile arrival counters
   // (one int per 128 columns, up to N = LLK_DECODE_NOALLOC_MAX_N) and at
@@ -195,6 +196,7 @@ extern "C" int llk_swiglu_decode_noalloc(const Tensor2D *x, const Tensor2D *wg, 
   if (cudaMemsetAsync(scratch + decode_counter_offset(M, N), 0, decode_counter_bytes(N), stream) != cudaSuccess)
     return LLK_ERR_CUDA;
   cudaError_t e =
-      decode_launch(tg, tu, tx, y->data, y->stride0, y_f32, M, N, K, scratch, device_status, d, 0, stream);
+      decode_launch(tg, tu, tx, y->data, y->stride0, y_f32, M, N, K, scratch, device_status, d, 0,
+                    gpu && gpu->math_mode != LLK_MATH_STRICT ? 1 : 0, stream);
   return e == cudaSuccess ? LLK_OK : LLK_ERR_CUDA;
 }

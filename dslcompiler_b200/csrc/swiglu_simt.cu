@@ -21,6 +21,8 @@ __device__ __forceinline__ float bf16_at(const uint16_t *p, int64_t i) {
 
 // One thread per output element; 32 consecutive columns per warp so the
 // weight reads of a warp are contiguous when the inner stride is 1.
+// MODE: 0 = SwiGLU (strict epilogue), 3 = SwiGLU (fast epilogue), 1 = matmul,
+// 2 = matmul accumulating into y.
 template <int MODE>
 __global__ void __launch_bounds__(256) simt_kernel(const uint16_t *__restrict__ x, int64_t ldx, int64_t sxk,
                                                    const uint16_t *__restrict__ wg, int64_t ldw, int64_t swn,
@@ -44,11 +46,11 @@ __global__ void __launch_bounds__(256) simt_kernel(const uint16_t *__restrict__ 
   for (int64_t k = 0; k < K; ++k) {
     const float xv = bf16_at(x, m * ldx + k * sxk);
     g = fmaf(xv, bf16_at(wg, wbase + k * wk), g);
-    if (MODE == 0) u = fmaf(xv, bf16_at(wu, wbase_u + k * wk_u), u);
+    if (MODE == 0 || MODE == 3) u = fmaf(xv, bf16_at(wu, wbase_u + k * wk_u), u);
   }
   float r;
-  if (MODE == 0) {
-    r = silu_mul(g, u);
+  if (MODE == 0 || MODE == 3) {
+    r = silu_mul_mode<MODE == 3>(g, u);
   } else {
     r = g;
   }
@@ -66,7 +68,8 @@ __global__ void __launch_bounds__(256) simt_kernel(const uint16_t *__restrict__ 
 
 cudaError_t simt_launch(int mode, const void *x, int64_t ldx, int64_t sxk, const void *wg, const void *wu,
                         int64_t ldw, int64_t swn, int64_t ldwu, int64_t swun, void *y, int64_t ldy, int64_t syn,
-                        int y_f32, int64_t M, int64_t N, int64_t K, int slab_major, cudaStream_t stream) {
+                        int y_f32, int64_t M, int64_t N, int64_t K, int slab_major, int fast_math,
+                        cudaStream_t stream) {
   if (M <= 0 || N <= 0) return cudaSuccess;
   if (M > 65535) return cudaErrorInvalidValue;
   dim3 block(256);
@@ -76,8 +79,12 @@ cudaError_t simt_launch(int mode, const void *x, int64_t ldx, int64_t sxk, const
   const uint16_t *up = static_cast<const uint16_t *>(wu);
   switch (mode) {
     case 0:
-      simt_kernel<0><<<grid, block, 0, stream>>>(xp, ldx, sxk, gp, ldw, swn, up, ldwu, swun, y, ldy, syn, y_f32, M, N,
-                                                 K, slab_major);
+      if (fast_math)
+        simt_kernel<3><<<grid, block, 0, stream>>>(xp, ldx, sxk, gp, ldw, swn, up, ldwu, swun, y, ldy, syn, y_f32, M,
+                                                   N, K, slab_major);
+      else
+        simt_kernel<0><<<grid, block, 0, stream>>>(xp, ldx, sxk, gp, ldw, swn, up, ldwu, swun, y, ldy, syn, y_f32, M,
+                                                   N, K, slab_major);
       break;
     case 1:
       simt_kernel<1><<<grid, block, 0, stream>>>(xp, ldx, sxk, gp, ldw, swn, gp, ldw, swn, y, ldy, syn, 1, M, N, K,

@@ -61,7 +61,9 @@ template <int MODE>
 __global__ void __launch_bounds__(kThreads, 1)
     tc_swiglu_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__ CUtensorMap tm_b0,
                      const __grid_constant__ CUtensorMap tm_b1, const TcParams p) {
-  constexpr bool kSwiglu = (MODE == TC_SWIGLU_BF16 || MODE == TC_SWIGLU_F32);
+  constexpr int kMode = MODE & ~TC_FAST_MATH;
+  constexpr bool kFast = (MODE & TC_FAST_MATH) != 0;
+  constexpr bool kSwiglu = (kMode == TC_SWIGLU_BF16 || kMode == TC_SWIGLU_F32);
   constexpr int kTileN = kSwiglu ? 128 : 256;  // output columns per tile
 
   extern __shared__ __align__(1024) uint8_t smem_raw[];
@@ -222,8 +224,8 @@ __global__ void __launch_bounds__(kThreads, 1)
           if (row < p.M && col < p.N) {
             float y[32];
 #pragma unroll
-            for (int j = 0; j < 32; ++j) y[j] = silu_mul(__uint_as_float(g[j]), __uint_as_float(u[j]));
-            if (MODE == TC_SWIGLU_BF16) {
+            for (int j = 0; j < 32; ++j) y[j] = silu_mul_mode<kFast>(__uint_as_float(g[j]), __uint_as_float(u[j]));
+            if (kMode == TC_SWIGLU_BF16) {
               uint16_t *dst = reinterpret_cast<uint16_t *>(p.y) + (int64_t)row * p.ldy + col;
               if (p.vec_ok && col + 32 <= p.N) {
                 uint4 *d4 = reinterpret_cast<uint4 *>(dst);
@@ -266,7 +268,7 @@ __global__ void __launch_bounds__(kThreads, 1)
               for (int v = 0; v < 8; ++v) {
                 float4 o = make_float4(__uint_as_float(r[4 * v]), __uint_as_float(r[4 * v + 1]),
                                        __uint_as_float(r[4 * v + 2]), __uint_as_float(r[4 * v + 3]));
-                if (MODE == TC_MATMUL_F32_ACC) {
+                if (kMode == TC_MATMUL_F32_ACC) {
                   float4 c4 = d4[v];
                   o.x += c4.x;
                   o.y += c4.y;
@@ -280,7 +282,7 @@ __global__ void __launch_bounds__(kThreads, 1)
               for (int j = 0; j < 32; ++j) {
                 if (col + j < p.N) {
                   float o = __uint_as_float(r[j]);
-                  if (MODE == TC_MATMUL_F32_ACC) o += dst[j];
+                  if (kMode == TC_MATMUL_F32_ACC) o += dst[j];
                   dst[j] = o;
                 }
               }
@@ -306,7 +308,10 @@ __global__ void __launch_bounds__(kThreads, 1)
 
 int tc_smem_bytes() { return kStages * kStageBytes + static_cast<int>(sizeof(SharedTail)) + 1024; }
 int tc_threads() { return kThreads; }
-int tc_tile_n(int mode) { return (mode == TC_SWIGLU_BF16 || mode == TC_SWIGLU_F32) ? 128 : 256; }
+int tc_tile_n(int mode) {
+  const int base = mode & ~TC_FAST_MATH;
+  return (base == TC_SWIGLU_BF16 || base == TC_SWIGLU_F32) ? 128 : 256;
+}
 
 template <int MODE>
 static cudaError_t launch_mode(const CUtensorMap &a, const CUtensorMap &b0, const CUtensorMap &b1, const TcParams &p,
@@ -346,6 +351,10 @@ cudaError_t tc_launch(int mode, const CUtensorMap &a, const CUtensorMap &b0, con
       return launch_mode<TC_SWIGLU_BF16>(a, b0, b1, p, grid, stream);
     case TC_SWIGLU_F32:
       return launch_mode<TC_SWIGLU_F32>(a, b0, b1, p, grid, stream);
+    case TC_SWIGLU_BF16 | TC_FAST_MATH:
+      return launch_mode<TC_SWIGLU_BF16 | TC_FAST_MATH>(a, b0, b1, p, grid, stream);
+    case TC_SWIGLU_F32 | TC_FAST_MATH:
+      return launch_mode<TC_SWIGLU_F32 | TC_FAST_MATH>(a, b0, b1, p, grid, stream);
     case TC_MATMUL_F32:
       return launch_mode<TC_MATMUL_F32>(a, b0, b1, p, grid, stream);
     case TC_MATMUL_F32_ACC:

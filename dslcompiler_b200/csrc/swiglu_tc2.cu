@@ -118,7 +118,9 @@ __device__ __forceinline__ bool item_to_work(const TcParams &p, int n_pairs, int
 template <int MODE>
 __device__ __forceinline__ bool ksplit_epilogue(const TcParams &p, const Work &w, int tl, uint32_t rank, int q,
                                                 int lane, uint32_t t_row, int m0, int n0, volatile int *abort) {
-  constexpr bool kSwiglu = (MODE == TC_SWIGLU_BF16 || MODE == TC_SWIGLU_F32);
+  constexpr int kMode = MODE & ~TC_FAST_MATH;
+  constexpr bool kFast = (MODE & TC_FAST_MATH) != 0;
+  constexpr bool kSwiglu = (kMode == TC_SWIGLU_BF16 || kMode == TC_SWIGLU_F32);
   constexpr int kChunks = kSwiglu ? 8 : 16;
   constexpr size_t kBlock = 64 * 128;  // float4s per partial block
   const int s = w.nparts;
@@ -215,10 +217,10 @@ __device__ __forceinline__ bool ksplit_epilogue(const TcParams &p, const Work &w
     if (kSwiglu) {
       float y[16];
 #pragma unroll
-      for (int j = 0; j < 16; ++j) y[j] = silu_mul(ga[j], ua[j]);
+      for (int j = 0; j < 16; ++j) y[j] = silu_mul_mode<kFast>(ga[j], ua[j]);
       for (int t = -1; t < p.n_peers; ++t) {
         void *base = t < 0 ? p.y : p.y_peers[t];
-        if (MODE == TC_SWIGLU_BF16) {
+        if (kMode == TC_SWIGLU_BF16) {
           uint16_t *dst = reinterpret_cast<uint16_t *>(base) + off;
           if (vec) {
             uint4 *d4 = reinterpret_cast<uint4 *>(dst);
@@ -250,7 +252,7 @@ __device__ __forceinline__ bool ksplit_epilogue(const TcParams &p, const Work &w
       for (int j = 0; j < 16; ++j) {
         if (col + j < p.N) {
           float o = ga[j];
-          if (MODE == TC_MATMUL_F32_ACC) o += dst[j];
+          if (kMode == TC_MATMUL_F32_ACC) o += dst[j];
           dst[j] = o;
           for (int t = 0; t < p.n_peers; ++t) reinterpret_cast<float *>(p.y_peers[t])[off + j] = o;
         }
@@ -372,7 +374,9 @@ __global__ void __launch_bounds__(kThreads, 1)
     tc2_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__ CUtensorMap tm_b0,
                const __grid_constant__ CUtensorMap tm_b1, const TcParams p,
                const __grid_constant__ YStoreMaps ym) {
-  constexpr bool kSwiglu = (MODE == TC_SWIGLU_BF16 || MODE == TC_SWIGLU_F32);
+  constexpr int kMode = MODE & ~TC_FAST_MATH;
+  constexpr bool kFast = (MODE & TC_FAST_MATH) != 0;
+  constexpr bool kSwiglu = (kMode == TC_SWIGLU_BF16 || kMode == TC_SWIGLU_F32);
   constexpr int kTileN = kSwiglu ? 128 : 256;
 
   extern __shared__ __align__(1024) uint8_t smem_raw[];
@@ -569,7 +573,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         // the map's swizzled layout (64-byte rows for bf16, 128-byte for
         // f32; the XOR keeps each 8-lane phase of the 16-byte stores on
         // distinct banks), then one lane stores it through every map.
-        constexpr bool kBf16 = (MODE == TC_SWIGLU_BF16);
+        constexpr bool kBf16 = (kMode == TC_SWIGLU_BF16);
         constexpr uint32_t kBuf = kBf16 ? 2048 : 4096;
         constexpr int kNBuf = kStagingPerWarp / kBuf;
         const uint32_t wstage = smem_u32(staging) + q * kStagingPerWarp;
@@ -584,9 +588,11 @@ __global__ void __launch_bounds__(kThreads, 1)
           if (r0 >= p.M || col >= p.N) continue;  // warp-uniform
           float y[32];
 #pragma unroll
-          for (int j = 0; j < 32; ++j) y[j] = silu_mul(__uint_as_float(g[j]), __uint_as_float(u[j]));
+          for (int j = 0; j < 32; ++j) y[j] = silu_mul_mode<kFast>(__uint_as_float(g[j]), __uint_as_float(u[j]));
           const uint32_t buf = wstage + static_cast<uint32_t>(y_chunks % kNBuf) * kBuf;
-          if (lane == 0) bulk_wait_group_read<kNBuf - 1>();
+          // lanes that store (one per map) wait until their store of this
+          // buffer's previous chunk has read it
+          if (lane < ym.n) bulk_wait_group_read<kNBuf - 1>();
           __syncwarp();
           if (kBf16) {
             const uint32_t rowa = buf + lane * 64;
@@ -607,8 +613,10 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
           fence_proxy_async_smem();
           __syncwarp();
-          if (lane == 0) {
-            for (int i = 0; i < ym.n; ++i) tma_store_2d(&ym.m[i], buf, ym.col0 + col, r0);
+          // one lane per map (this GPU's Y, then each peer's): the stores to
+          // the GPUs go out side by side instead of one after another
+          if (lane < ym.n) {
+            tma_store_2d(&ym.m[lane], buf, ym.col0 + col, r0);
             bulk_commit_group();
           }
           ++y_chunks;
@@ -624,10 +632,10 @@ __global__ void __launch_bounds__(kThreads, 1)
           if (row < p.M && col < p.N) {
             float y[32];
 #pragma unroll
-            for (int j = 0; j < 32; ++j) y[j] = silu_mul(__uint_as_float(g[j]), __uint_as_float(u[j]));
+            for (int j = 0; j < 32; ++j) y[j] = silu_mul_mode<kFast>(__uint_as_float(g[j]), __uint_as_float(u[j]));
             const int64_t off = (int64_t)row * p.ldy + col;
             const bool vec = p.vec_ok && col + 32 <= p.N;
-            if (MODE == TC_SWIGLU_BF16) {
+            if (kMode == TC_SWIGLU_BF16) {
               uint32_t pk[16];
 #pragma unroll
               for (int j = 0; j < 16; ++j) pk[j] = pack_bf16x2(y[2 * j], y[2 * j + 1]);
@@ -677,7 +685,7 @@ __global__ void __launch_bounds__(kThreads, 1)
               for (int v = 0; v < 8; ++v) {
                 float4 o = make_float4(__uint_as_float(r[4 * v]), __uint_as_float(r[4 * v + 1]),
                                        __uint_as_float(r[4 * v + 2]), __uint_as_float(r[4 * v + 3]));
-                if (MODE == TC_MATMUL_F32_ACC) {
+                if (kMode == TC_MATMUL_F32_ACC) {
                   const float4 c4 = d4[v];
                   o.x += c4.x;
                   o.y += c4.y;
@@ -692,7 +700,7 @@ __global__ void __launch_bounds__(kThreads, 1)
               for (int j = 0; j < 32; ++j) {
                 if (col + j < p.N) {
                   float o = __uint_as_float(r[j]);
-                  if (MODE == TC_MATMUL_F32_ACC) o += dst[j];
+                  if (kMode == TC_MATMUL_F32_ACC) o += dst[j];
                   dst[j] = o;
                   for (int t = 0; t < p.n_peers; ++t) reinterpret_cast<float *>(p.y_peers[t])[off + j] = o;
                 }
@@ -704,7 +712,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       tc_fence_before();
       mbar_arrive_cluster(leader_tmem_empty + acc * 8u);
     }
-    if (ym.n > 0 && lane == 0) bulk_wait_group_all();  // staging is read and the stores done before exit
+    if (lane < ym.n) bulk_wait_group_all();  // staging is read and the stores done before exit
   }
 
   tc_fence_before();
@@ -866,6 +874,12 @@ cudaError_t tc2_launch(int mode, const CUtensorMap &a, const CUtensorMap &b0, co
     case TC_SWIGLU_F32:
       return launch_pair_mode<TC_SWIGLU_F32>(a, b0, b1, p, max_pairs, tail_split, sched_counter, workspace,
                                              workspace_bytes, stream, m);
+    case TC_SWIGLU_BF16 | TC_FAST_MATH:
+      return launch_pair_mode<TC_SWIGLU_BF16 | TC_FAST_MATH>(a, b0, b1, p, max_pairs, tail_split, sched_counter,
+                                                             workspace, workspace_bytes, stream, m);
+    case TC_SWIGLU_F32 | TC_FAST_MATH:
+      return launch_pair_mode<TC_SWIGLU_F32 | TC_FAST_MATH>(a, b0, b1, p, max_pairs, tail_split, sched_counter,
+                                                            workspace, workspace_bytes, stream, m);
     case TC_MATMUL_F32:
       return launch_pair_mode<TC_MATMUL_F32>(a, b0, b1, p, max_pairs, tail_split, sched_counter, workspace,
                                              workspace_bytes, stream, kNoMaps);

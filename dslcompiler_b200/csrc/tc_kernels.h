@@ -10,6 +10,10 @@ namespace llk_b200 {
 
 // Output modes of the tcgen05 kernel.
 enum TcMode { TC_SWIGLU_BF16 = 0, TC_SWIGLU_F32 = 1, TC_MATMUL_F32 = 2, TC_MATMUL_F32_ACC = 3 };
+// Flag or-ed into a SwiGLU mode: the fast epilogue (__expf, __fdividef:
+// math_mode bounded_fast / unsafe_fast) instead of the strict one (expf and
+// an IEEE division).  Each combination is its own kernel instantiation.
+constexpr int TC_FAST_MATH = 8;
 
 struct TcParams {
   int M, N, K;        // problem: Y[M,N], reduction K
@@ -99,10 +103,12 @@ cudaError_t tc_launch(int mode, const CUtensorMap &a, const CUtensorMap &b0, con
 // CUDA-core kernel for any strides / alignment (small or odd shapes).
 // x, wg, wu bf16; y bf16 (y_f32 == 0) or f32.  mode 0 = swiglu, 1 = matmul,
 // 2 = matmul accumulating into y.  slab_major: wg/wu are slab-major packed
-// weights ([N/64][K][64]; ld/stride arguments ignored).
+// weights ([N/64][K][64]; ld/stride arguments ignored).  fast_math: the fast
+// SwiGLU epilogue instead of the strict one.
 cudaError_t simt_launch(int mode, const void *x, int64_t ldx, int64_t sxk, const void *wg, const void *wu,
                         int64_t ldw, int64_t swn, int64_t ldwu, int64_t swun, void *y, int64_t ldy, int64_t syn,
-                        int y_f32, int64_t M, int64_t N, int64_t K, int slab_major, cudaStream_t stream);
+                        int y_f32, int64_t M, int64_t N, int64_t K, int slab_major, int fast_math,
+                        cudaStream_t stream);
 
 // Diagnostic: a bounded wait that is made to expire (see swiglu_simt.cu).
 cudaError_t diag_timeout_launch(int *status, uint64_t limit_ns, cudaStream_t stream);

@@ -116,8 +116,10 @@ def entry_key(e: ScheduleEntry):
 
     variant = e.schedule.get("variant", "tc")
     v = capi.VARIANTS[variant] if isinstance(variant, str) else int(variant)
+    math = capi.MATH_MODES.get(e.math_mode, capi.LLK_MATH_STRICT) if e.operation == "fused_swiglu" else \
+        capi.LLK_MATH_STRICT
     return KernelKey(operation=OPS[e.operation], output_type=DTYPES.get(e.dtype, capi.LLK_DTYPE_BF16),
-                     M_bucket=e.M_bucket, N=e.N, K=e.K, thread_count=v)
+                     M_bucket=e.M_bucket, N=e.N, K=e.K, thread_count=v, math_mode=math)
 
 
 def entry_plan(e: ScheduleEntry) -> dict:

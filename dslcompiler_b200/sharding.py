@@ -117,8 +117,10 @@ class PeerGroupSwiGLU:
     """
 
     def __init__(self, wg, wu, N: int, max_rows: int, *, out_dtype: str = "bf16", group=None,
-                 already_sharded: bool = False, pack: bool = True, device: int | None = None):
+                 already_sharded: bool = False, pack: bool = True, device: int | None = None,
+                 math_mode: str = "strict"):
         self.group = group
+        self.math_mode = math_mode
         self.rank = dist.get_rank(group) if dist and dist.is_initialized() else 0
         self.world = dist.get_world_size(group) if dist and dist.is_initialized() else 1
         self.N, self.max_rows = N, max_rows
@@ -167,7 +169,8 @@ class PeerGroupSwiGLU:
         if M > self.max_rows:
             raise ValueError(f"M = {M} exceeds the group's max_rows = {self.max_rows}")
         st = stream if stream is not None else torch.cuda.current_stream(self.device).cuda_stream
-        g = gpu_context(self.device, st, capi.LLK_DTYPE_FP32 if self.f32 else capi.LLK_DTYPE_BF16)
+        g = gpu_context(self.device, st, capi.LLK_DTYPE_FP32 if self.f32 else capi.LLK_DTYPE_BF16,
+                        math_mode=self.math_mode)
         tx = tensor2d(x)
         if self._packed is not None:
             rc = lib().llk_swiglu_column_parallel(ctypes.byref(tx), None, None, self._packed._h, self.N, self._h,

@@ -61,7 +61,8 @@ def _device_of(t, device):
     return -1
 
 
-def gpu_context(device=-1, stream=None, y_dtype=capi.LLK_DTYPE_BF16, variant="auto") -> GpuContext:
+def gpu_context(device=-1, stream=None, y_dtype=capi.LLK_DTYPE_BF16, variant="auto",
+                math_mode="strict") -> GpuContext:
     g = GpuContext()
     g.device = device
     g.stream = stream
@@ -69,6 +70,9 @@ def gpu_context(device=-1, stream=None, y_dtype=capi.LLK_DTYPE_BF16, variant="au
     if variant not in capi.VARIANTS:
         raise ValueError(f"variant must be one of {sorted(capi.VARIANTS)}")
     g.variant = capi.VARIANTS[variant]
+    if math_mode not in capi.MATH_MODES:
+        raise ValueError(f"math_mode must be one of {sorted(capi.MATH_MODES)}")
+    g.math_mode = capi.MATH_MODES[math_mode]
     return g
 
 
@@ -90,9 +94,11 @@ def _new_out(like, rows, cols, f32: bool):
 
 
 def fused_swiglu(x, wg, wu, *, out=None, out_dtype: str = "bf16", variant: str = "auto", stream=None,
-                 device=None, scratch=None):
+                 device=None, scratch=None, math_mode: str = "strict"):
     """Y = SiLU(X Wg) * (X Wu) on the B200.  out_dtype: 'bf16' (the op
-    contract) or 'f32'.  Returns Y (``out`` when given)."""
+    contract) or 'f32'.  math_mode: 'strict' (accurate exp, IEEE division:
+    the fused lowering's epilogue), 'bounded_fast' or 'unsafe_fast' (the
+    hardware's approximate exp and division).  Returns Y (``out`` when given)."""
     _check_bf16(x, wg, wu)
     f32 = out_dtype in ("f32", "fp32", "float32")
     if out is None:
@@ -102,7 +108,7 @@ def fused_swiglu(x, wg, wu, *, out=None, out_dtype: str = "bf16", variant: str =
     if scratch is not None:
         ctx = KernelContext(scratch.data_ptr(), scratch.numel() * scratch.element_size())
     g = gpu_context(_device_of(x, device), _stream_of(x, stream),
-                    capi.LLK_DTYPE_FP32 if f32 else capi.LLK_DTYPE_BF16, variant)
+                    capi.LLK_DTYPE_FP32 if f32 else capi.LLK_DTYPE_BF16, variant, math_mode)
     check(lib().llk_swiglu_ex(ctypes.byref(tx), ctypes.byref(tg), ctypes.byref(tu), ctypes.byref(ty),
                               ctypes.byref(ctx), ctypes.byref(g)), "llk_swiglu_ex")
     return out
@@ -191,13 +197,15 @@ class PackedWeights:
         g = gpu_context(-1, _stream_of(wg, stream))
         check(lib().llk_repack(self._h, ctypes.byref(tg), ctypes.byref(tu), ctypes.byref(g)), "llk_repack")
 
-    def __call__(self, x, *, out=None, out_dtype: str = "bf16", variant: str = "auto", stream=None):
+    def __call__(self, x, *, out=None, out_dtype: str = "bf16", variant: str = "auto", stream=None,
+                 math_mode: str = "strict"):
         _check_bf16(x)
         f32 = out_dtype in ("f32", "fp32", "float32")
         if out is None:
             out = _new_out(x, x.shape[0], self.N, f32)
         tx, ty = tensor2d(x), tensor2d(out)
-        g = gpu_context(-1, _stream_of(x, stream), capi.LLK_DTYPE_FP32 if f32 else capi.LLK_DTYPE_BF16, variant)
+        g = gpu_context(-1, _stream_of(x, stream), capi.LLK_DTYPE_FP32 if f32 else capi.LLK_DTYPE_BF16, variant,
+                        math_mode)
         check(lib().llk_swiglu_packed(ctypes.byref(tx), self._h, ctypes.byref(ty), None, ctypes.byref(g)),
               "llk_swiglu_packed")
         return out

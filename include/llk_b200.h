@@ -99,14 +99,24 @@ enum llk_variant {
   LLK_VARIANT_SIMT = 3    /* CUDA-core kernel for any stride/alignment */
 };
 
+/* The SiLU epilogue's numerics (include/LLK/Runtime/KernelKey.h:39 MathMode,
+ * the op's math_mode attribute).  STRICT: sigmoid = 1 / (1 + exp(-g)) with
+ * an accurate exp and an IEEE-rounded division, the fused lowering's
+ * sequence (lib/Transforms/FuseDoubleContraction.cpp:189-196).  The fast
+ * modes use the hardware's approximate exp and division (about 2 ulp each);
+ * BOUNDED_FAST and UNSAFE_FAST run the same kernels here. */
+enum llk_math_mode { LLK_MATH_STRICT = 0, LLK_MATH_BOUNDED_FAST = 1, LLK_MATH_UNSAFE_FAST = 2 };
+
 /* GPU-side call options, carried beside (not inside) KernelContext so that
- * struct keeps the reference's 16-byte layout. */
+ * struct keeps the reference's 16-byte layout.  Zero-filled = current
+ * device, default stream, bf16 Y, automatic kernel choice, strict math. */
 typedef struct llk_gpu_context {
   int device;      /* CUDA ordinal the pointers live on; -1 = current */
   void *stream;    /* cudaStream_t; NULL = legacy default stream */
   int y_dtype;     /* enum llk_dtype: BF16 (op contract) or FP32 */
   int variant;     /* enum llk_variant */
-  int reserved[4]; /* must be zero */
+  int math_mode;   /* enum llk_math_mode (SwiGLU epilogue; matmul ignores it) */
+  int reserved[3]; /* must be zero */
 } llk_gpu_context;
 
 /* ---- entry points ------------------------------------------------------ */

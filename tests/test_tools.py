@@ -243,3 +243,82 @@ def test_micro_mma_verifier_messages(tmp_path):
     bad.write_text(base.format(**dict(ok, a="64x128xbf16")))
     r = _run(["dslcompiler_b200.cli.micro_perf", str(bad)])
     assert r.returncode == 1 and "lhs tile shape must be [M, K]" in r.stderr
+
+
+# ------------------------------------------------ micro.kernel dispatch records
+GENERIC = """
+// the generic form of the same op, split over lines, attributes reordered
+%y = "llk.fused_swiglu"(%x, %wg, %wu, %init)
+     {math_mode = #llk.math_mode<unsafe_fast>, accumulator_type = f32}
+     : (tensor<300x512xbf16>, tensor<512x640xbf16>, tensor<512x640xbf16>,
+        tensor<300x640xf32>) -> tensor<300x640xf32>
+"""
+
+
+def test_parse_generic_form_and_math_mode():
+    op = compiler.parse_llk(GENERIC)[0]
+    compiler.verify(op)
+    assert op.operands == ["%x", "%wg", "%wu", "%init"]
+    assert compiler.resolve_shape(op) == (300, 640, 512)
+    assert compiler.op_math_mode(op) == "unsafe_fast"
+    assert compiler.op_math_mode(compiler.parse_llk(SWIGLU.format(M=8, K=64, N=128, N2=128))[0]) == "bounded_fast"
+
+
+@pytest.mark.parametrize("M,K,N", [(2048, 4096, 11008), (300, 512, 640), (1, 4096, 14336)])
+def test_micro_kernel_round_trip_to_dispatch_record(M, K, N):
+    from dslcompiler_b200 import micro
+
+    op = compiler.parse_llk(SWIGLU.format(M=M, K=K, N=N, N2=N))[0]
+    low = compiler.lower_to_micro(op, M, N, K)
+    assert compiler.verify_micro(low.text) == []
+    k = micro.parse_micro_kernel(low.text)
+    assert (k.M, k.N, k.K, k.op) == (M, N, K, "fused_swiglu")
+    assert k.math_mode == "bounded_fast" and k.y_dtype == "bf16"
+    assert k.plan == {f: low.plan[f] for f in k.plan}  # every launch-plan field survives the text
+    assert k.variant == ("decode" if M <= 16 else "tc")
+    # reformatting (line breaks, attribute order) does not change the record
+    head, rest = low.text.split("attributes {", 1)
+    attrs, body = rest.split("} {", 1)
+    swapped = head + "attributes {\n  " + ",\n  ".join(reversed(attrs.split(", "))) + "\n} {" + body
+    assert micro.parse_micro_kernel(swapped).plan == k.plan
+
+
+def test_micro_kernel_refuses_foreign_targets():
+    from dslcompiler_b200 import micro
+
+    op = compiler.parse_llk(SWIGLU.format(M=256, K=512, N=384, N2=384))[0]
+    text = compiler.lower_to_micro(op, 256, 384, 512).text
+    with pytest.raises(micro.MicroError, match="target"):
+        micro.parse_micro_kernel(text.replace('"b200-sm100a"', '"avx2"'))
+    with pytest.raises(micro.MicroError, match="candidate"):
+        micro.parse_micro_kernel(text.replace('candidate = "tc2_kernel<swiglu>"', 'candidate = "avx2_kernel"'))
+
+
+def test_search_space_emit_parse_and_candidates(tmp_path):
+    from dslcompiler_b200 import micro
+
+    for op, M, N, K in [("fused_swiglu", 2048, 11008, 4096), ("fused_swiglu", 4, 1792, 4096),
+                        ("matmul", 4096, 4096, 4096)]:
+        sp = micro.search_space(op, M, N, K)
+        text = micro.emit_search_space(sp)
+        assert text.startswith(f"micro.search_space @{op}_M{M}_N{N}_K{K}_space")
+        back = micro.parse_search_space(text)
+        assert back.params == sp.params and [c[0] for c in back.constraints] == [c[0] for c in sp.constraints]
+        cands = micro.candidates(back)
+        pair = {"candidate": "tc2_kernel", "BM": 256, "BN": sp.params["BN"][0], "BK": 64, "num_stages": 6,
+                "grid": 148, "tail_split": 0, "sched": 1}
+        assert cands and micro.legal(sp, pair)[0] == (M > 128)
+        # the K-split tail needs the static schedule; pairs need M > 128
+        assert not any(c["split_k"] < 0 and c["sched"] == 0 for c in cands)
+        if M <= 128:
+            assert not any(c["block_m"] == 256 for c in cands)
+    f = tmp_path / "in.mlir"
+    f.write_text(SWIGLU.format(M=2048, K=4096, N=11008, N2=11008))
+    r = _run(["dslcompiler_b200.cli.llk_compile", str(f), "--emit", "micro-search-space"])
+    assert r.returncode == 0 and "micro.search_space @fused_swiglu_M2048_N11008_K4096_space" in r.stdout
+    space = tmp_path / "space.mlir"
+    space.write_text(r.stdout.replace("Compilation successful", ""))
+    out = tmp_path / "tune.json"
+    r = _run(["dslcompiler_b200.cli.llk_tune", "--M", "2048", "--N", "11008", "--K", "4096", "--dry-run",
+              "--search-space", str(space), "-o", str(out)])
+    assert r.returncode == 0 and "Wrote top-3 configs" in r.stdout, r.stderr
