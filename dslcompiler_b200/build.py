@@ -24,8 +24,10 @@ OUT_DIR = os.path.join(PKG, "lib")
 OBJ_DIR = os.path.join(ROOT, "_build", "obj")
 LIB = os.path.join(OUT_DIR, "libllk_b200.so")
 
-SOURCES = ["swiglu_tc.cu", "swiglu_tc2.cu", "swiglu_decode.cu", "swiglu_simt.cu", "llk_runtime.cu", "swiglu_decode_noalloc.cu", "shard_gather.cu"]
-HEADERS = ["sm100_ptx.cuh", "tc_kernels.h", "decode_kernels.h", "workspace.h"]
+SOURCES = ["swiglu_tc.cu", "swiglu_tc2.cu", "swiglu_decode.cu", "swiglu_simt.cu", "llk_runtime.cu", "swiglu_decode_noalloc.cu", "shard_gather.cu",
+           "rope_attention.cu"]
+HEADERS = ["sm100_ptx.cuh", "tc_kernels.h", "decode_kernels.h", "workspace.h",
+           "attention_kernels.h"]
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 FLAGS = ["-O3", "-std=c++17", "-lineinfo", "-Xcompiler", "-fPIC",
           "-I" + os.path.join(ROOT, "include"), "-I" + CSRC]

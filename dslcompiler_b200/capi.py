@@ -114,6 +114,8 @@ PROTOTYPES = {
                            _P(GpuContext)]),
     "llk_swiglu_memref": (None, [_P(MemRef2D)] * 5),
     "llk_matmul": (_i, [_P(Tensor2D), _P(Tensor2D), _P(Tensor2D), _i, _P(KernelContext), _P(GpuContext)]),
+    "llk_rope": (_i, [_vp, _vp, _vp, _i64, _i64, _i64, _i64, ctypes.c_double, _P(GpuContext)]),
+    "llk_attention": (_i, [_vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _i64, ctypes.c_float, _i, _P(GpuContext)]),
     "llk_last_status": (_i, []),
     "llk_status_string": (ctypes.c_char_p, [_i]),
     "llk_synchronize": (_i, [_i, _vp]),

@@ -14,12 +14,14 @@
 #include <cstdint>
 #include <cstdlib>
 #include <cstring>
+#include <functional>
 #include <list>
 #include <mutex>
 #include <string>
 #include <unordered_map>
 #include <vector>
 
+#include "attention_kernels.h"
 #include "decode_kernels.h"
 #include "llk_b200.h"
 #include "tc_kernels.h"
@@ -85,6 +87,22 @@ int resolve_device(const llk_gpu_context *gpu, int *dev_out) {
   *dev_out = dev;
   return LLK_OK;
 }
+
+// Puts the caller's current device back when an entry point returns
+// (device_init makes the call's device current).
+struct DeviceRestore {
+  int prev = -1;
+  DeviceRestore() {
+    if (cudaGetDevice(&prev) != cudaSuccess) {
+      cudaGetLastError();
+      prev = -1;
+    }
+  }
+  ~DeviceRestore() {
+    int cur = -1;
+    if (prev >= 0 && cudaGetDevice(&cur) == cudaSuccess && cur != prev) cudaSetDevice(prev);
+  }
+};
 
 // Makes `dev` current and initialises its state once.
 int device_init(int dev, DeviceState **out) {
@@ -699,6 +717,7 @@ int swiglu_host_pipelined(DeviceState &ds, const Tensor2D *x, const Tensor2D *wg
 int run_op(int op, const Tensor2D *x, const Tensor2D *wg, const Tensor2D *wu, Tensor2D *y, int y_f32, int accumulate,
            KernelContext *ctx, const llk_gpu_context *gpu, const DevTensor *packed_g = nullptr,
            const DevTensor *packed_u = nullptr) {
+  DeviceRestore restore;
   if (gpu && (gpu->y_dtype != LLK_DTYPE_BF16 && gpu->y_dtype != LLK_DTYPE_FP32)) return LLK_ERR_ARG;
   if (gpu && (gpu->variant < LLK_VARIANT_AUTO || gpu->variant > LLK_VARIANT_SIMT)) return LLK_ERR_ARG;
   if (gpu && (gpu->math_mode < LLK_MATH_STRICT || gpu->math_mode > LLK_MATH_UNSAFE_FAST)) return LLK_ERR_ARG;
@@ -905,7 +924,92 @@ int llk_matmul(const Tensor2D *a, const Tensor2D *b, Tensor2D *c, int accumulate
   return run_op(LLK_OP_MATMUL, a, b, b, c, 1, accumulate ? 1 : 0, ctx, gpu);
 }
 
+// ------------------------------------------------- llk.rope / llk.attention
+// Flat f32 / i64 arrays in host or device memory: host arrays are staged
+// through the device (the call then returns with the result on the host),
+// device arrays must live on the call's device.
+namespace {
+struct FlatArg {
+  const void *p;
+  int64_t n;     // elements
+  int elem;      // bytes per element
+  bool out;      // written by the kernel
+  bool in;       // read by the kernel
+};
+
+int run_flat(const llk_gpu_context *gpu, FlatArg *args, int nargs,
+             const std::function<cudaError_t(void **, cudaStream_t, bool)> &launch) {
+  DeviceRestore restore;
+  if (gpu && (gpu->math_mode < LLK_MATH_STRICT || gpu->math_mode > LLK_MATH_UNSAFE_FAST)) return LLK_ERR_ARG;
+  int dev, rc;
+  if ((rc = resolve_device(gpu, &dev)) != LLK_OK) return rc;
+  DeviceState *ds;
+  if ((rc = device_init(dev, &ds)) != LLK_OK) return rc;
+  cudaStream_t stream = gpu ? static_cast<cudaStream_t>(gpu->stream) : nullptr;
+  const bool fast = gpu && gpu->math_mode != LLK_MATH_STRICT;
+  std::lock_guard<std::mutex> lk(ds->mu);
+  Tensor2D views[4];
+  Staged st[4];
+  void *ptrs[4] = {};
+  bool any_host = false;
+  for (int i = 0; i < nargs; ++i) {
+    if (args[i].n > 0 && args[i].p == nullptr) return LLK_ERR_ARG;
+    const bool on_dev = args[i].n == 0 || is_device_ptr(args[i].p);
+    if (on_dev && args[i].n > 0 && on_other_device(args[i].p, dev)) return LLK_ERR_ARG;
+    views[i] = {const_cast<void *>(args[i].p), 1, args[i].n, args[i].n, 1};
+    if ((rc = stage_in(&views[i], on_dev, args[i].elem, ds->stage[i], args[i].in, stream, &st[i])) != LLK_OK)
+      return rc;
+    ptrs[i] = const_cast<void *>(st[i].t.data);
+    any_host = any_host || st[i].host;
+  }
+  if (launch(ptrs, stream, fast) != cudaSuccess) return LLK_ERR_CUDA;
+  for (int i = 0; i < nargs; ++i)
+    if (args[i].out && (rc = stage_out(st[i], args[i].elem, stream)) != LLK_OK) return rc;
+  if (any_host) return read_and_clear_status(*ds, stream);
+  return LLK_OK;
+}
+}  // namespace
+
+int llk_rope(const float *x, const int64_t *position_ids, float *y, int64_t B, int64_t H, int64_t L, int64_t D,
+             double theta, const llk_gpu_context *gpu) {
+  if (B < 0 || H < 0 || L < 0 || D < 0) return LLK_ERR_SHAPE;
+  if (D % 2 != 0) return LLK_ERR_SHAPE;  // pairs of dimensions
+  if (!rope_supported(B, H, L, D > 0 ? D : 2)) return LLK_ERR_UNSUPPORTED;
+  const int64_t n = B * H * L * D;
+  if (n == 0) return LLK_OK;
+  if (!(theta > 0.0)) return LLK_ERR_ARG;
+  FlatArg a[3] = {{x, n, 4, false, true}, {position_ids, L, 8, false, true}, {y, n, 4, true, x == y}};
+  if (x == y) {
+    // in place: one buffer, read and written
+    FlatArg b[2] = {{x, n, 4, true, true}, {position_ids, L, 8, false, true}};
+    return run_flat(gpu, b, 2, [&](void **p, cudaStream_t s, bool fast) {
+      return rope_launch(static_cast<float *>(p[0]), static_cast<const int64_t *>(p[1]), static_cast<float *>(p[0]),
+                         B, H, L, D, theta, fast ? 1 : 0, s);
+    });
+  }
+  return run_flat(gpu, a, 3, [&](void **p, cudaStream_t s, bool fast) {
+    return rope_launch(static_cast<const float *>(p[0]), static_cast<const int64_t *>(p[1]), static_cast<float *>(p[2]),
+                       B, H, L, D, theta, fast ? 1 : 0, s);
+  });
+}
+
+int llk_attention(const float *q, const float *k, const float *v, float *o, int64_t B, int64_t H, int64_t Lq,
+                  int64_t Lk, int64_t D, float scale, int causal, const llk_gpu_context *gpu) {
+  if (B < 0 || H < 0 || Lq < 0 || Lk < 0 || D < 0) return LLK_ERR_SHAPE;
+  if (B * H * Lq * D == 0) return LLK_OK;
+  if (!attention_supported(B, H, Lq, Lk, D)) return LLK_ERR_UNSUPPORTED;
+  if (o == q || o == k || o == v) return LLK_ERR_ARG;  // O accumulates while Q, K, V are read
+  const int64_t nq = B * H * Lq * D, nk = B * H * Lk * D;
+  FlatArg a[4] = {{q, nq, 4, false, true}, {k, nk, 4, false, true}, {v, nk, 4, false, true}, {o, nq, 4, true, true}};
+  return run_flat(gpu, a, 4, [&](void **p, cudaStream_t s, bool fast) {
+    return attention_launch(static_cast<const float *>(p[0]), static_cast<const float *>(p[1]),
+                            static_cast<const float *>(p[2]), static_cast<float *>(p[3]), B, H, Lq, Lk, D, scale,
+                            causal ? 1 : 0, fast ? 1 : 0, s);
+  });
+}
+
 int llk_synchronize(int device, void *stream) {
+  DeviceRestore restore;
   llk_gpu_context g;
   std::memset(&g, 0, sizeof(g));
   g.device = device;
@@ -918,6 +1022,7 @@ int llk_synchronize(int device, void *stream) {
 
 int llk_diag_timeout_probe(int device, int64_t limit_ns) {
   if (limit_ns <= 0) return LLK_ERR_ARG;
+  DeviceRestore restore;
   llk_gpu_context g;
   std::memset(&g, 0, sizeof(g));
   g.device = device;
@@ -1447,6 +1552,8 @@ int llk_swiglu_column_parallel(const Tensor2D *x, const Tensor2D *wg_shard, cons
                                const llk_gpu_context *gpu) {
   if (!x || !g || (!pw_shard && (!wg_shard || !wu_shard)) || N < 0) return LLK_ERR_ARG;
   if (!g->connected) return LLK_ERR_ARG;
+  if (gpu && (gpu->math_mode < LLK_MATH_STRICT || gpu->math_mode > LLK_MATH_UNSAFE_FAST)) return LLK_ERR_ARG;
+  DeviceRestore restore;
   if (gpu && gpu->device >= 0 && gpu->device != g->device) return LLK_ERR_ARG;
   const int y_f32 = (gpu && gpu->y_dtype == LLK_DTYPE_FP32) ? 1 : 0;
   if (gpu && gpu->y_dtype != LLK_DTYPE_BF16 && gpu->y_dtype != LLK_DTYPE_FP32) return LLK_ERR_ARG;

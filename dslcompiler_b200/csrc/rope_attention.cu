@@ -1,0 +1,406 @@
+// rope_attention.cu -- the llk.rope and llk.attention ops on sm_100a.
+//
+// Both ops are f32 in the reference (include/LLK/Dialect/LLKOps.td:69-131)
+// and lowered by lib/Conversion/LLKToLinalg/LLKToLinalg.cpp:162-615; these
+// kernels compute the same results on the GPU.
+//
+// RoPE (x [B,H,L,D] f32, position_ids [L] i64, theta):
+//   freq[i] = theta^(-2i/D) (f64), angle[p,i] = pos[p] * freq[i] (f64),
+//   c, s = cos / sin of the angle rounded to f32,
+//   y[2i] = x[2i]*c - x[2i+1]*s,  y[2i+1] = x[2i+1]*c + x[2i]*s  (f32, each
+//   product and sum rounded on its own, as the unfused arith ops are).
+// HBM-bound: a CTA takes a block of positions, builds their cos/sin table in
+// shared memory once, then streams those positions' rows of every (b, h)
+// with 16-byte loads and stores.
+//
+// Attention (q [B,H,Lq,D], k/v [B,H,Lk,D] f32, scale, causal):
+//   O = init + softmax(scale * Q K^T, masked where k > q when causal) V.
+// The reference materialises the [Lq, Lk] scores and runs a 3-pass stable
+// softmax; this kernel keeps a 64-row query tile on chip and sweeps 64-row
+// key tiles with the online (running max / running sum) form of the same
+// softmax -- identical in exact arithmetic, f32 rounding aside.  f32 inputs
+// and f32 accumulation on the CUDA cores (the op is f32; tensor-core tf32
+// would drop 13 mantissa bits of every product).
+#include <cuda.h>
+#include <cuda_runtime.h>
+
+#include <cmath>
+#include <cstdint>
+
+#include "attention_kernels.h"
+#include "sm100_ptx.cuh"
+
+namespace llk_b200 {
+
+namespace {
+
+// ------------------------------------------------------------------- RoPE
+constexpr int kRopeThreads = 256;
+constexpr int kRopeTableBytes = 48 * 1024;
+
+template <bool kFast>
+__device__ __forceinline__ void sincos_mode(float a, float *s, float *c) {
+  if constexpr (kFast) {
+    *s = __sinf(a);
+    *c = __cosf(a);
+  } else {
+    *s = sinf(a);
+    *c = cosf(a);
+  }
+}
+
+// Rotation of one (even, odd) pair with unfused f32 multiplies and adds.
+__device__ __forceinline__ float2 rotate(float e, float o, float c, float s) {
+  return make_float2(__fsub_rn(__fmul_rn(e, c), __fmul_rn(o, s)), __fadd_rn(__fmul_rn(o, c), __fmul_rn(e, s)));
+}
+
+// Grid: one CTA per block of P positions.  Shared memory: the block's
+// (cos, sin) table [P][D/2] as float2.
+template <bool kFast>
+__global__ void __launch_bounds__(kRopeThreads) rope_kernel(const float *__restrict__ x,
+                                                           const int64_t *__restrict__ pos, float *__restrict__ y,
+                                                           int64_t BH, int64_t L, int D, int P, double theta) {
+  extern __shared__ float2 table[];
+  const int half = D / 2;
+  const int64_t p0 = static_cast<int64_t>(blockIdx.x) * P;
+  const int np = static_cast<int>(L - p0 < P ? L - p0 : P);
+  pdl_launch_dependents();
+  pdl_wait();
+  for (int e = threadIdx.x; e < np * half; e += blockDim.x) {
+    const int pi = e / half, i = e % half;
+    const double freq = pow(theta, (-2.0 * static_cast<double>(i)) / static_cast<double>(D));
+    const double angle = static_cast<double>(pos[p0 + pi]) * freq;
+    float s, c;
+    sincos_mode<kFast>(static_cast<float>(angle), &s, &c);
+    table[e] = make_float2(c, s);
+  }
+  __syncthreads();
+  // The block's rows of one (b, h) are np * D contiguous floats.
+  const int64_t row_elems = static_cast<int64_t>(np) * D;
+  if ((D & 3) == 0) {
+    const int n4 = static_cast<int>(row_elems / 4);
+    for (int64_t bh = 0; bh < BH; ++bh) {
+      const int64_t base = (bh * L + p0) * D;
+      const float4 *src = reinterpret_cast<const float4 *>(x + base);
+      float4 *dst = reinterpret_cast<float4 *>(y + base);
+      for (int v = threadIdx.x; v < n4; v += blockDim.x) {
+        const float4 a = __ldcs(src + v);
+        const int e = v * 4;                   // element in the block
+        const int pi = e / D, i = (e % D) / 2;  // pair index of a.x, a.y
+        const float2 cs0 = table[pi * half + i], cs1 = table[pi * half + i + 1];
+        const float2 r0 = rotate(a.x, a.y, cs0.x, cs0.y), r1 = rotate(a.z, a.w, cs1.x, cs1.y);
+        __stcs(dst + v, make_float4(r0.x, r0.y, r1.x, r1.y));
+      }
+    }
+  } else {
+    const int n2 = static_cast<int>(row_elems / 2);
+    for (int64_t bh = 0; bh < BH; ++bh) {
+      const int64_t base = (bh * L + p0) * D;
+      const float2 *src = reinterpret_cast<const float2 *>(x + base);
+      float2 *dst = reinterpret_cast<float2 *>(y + base);
+      for (int v = threadIdx.x; v < n2; v += blockDim.x) {
+        const float2 a = src[v];
+        const int pi = (v * 2) / D, i = ((v * 2) % D) / 2;
+        const float2 cs = table[pi * half + i];
+        dst[v] = rotate(a.x, a.y, cs.x, cs.y);
+      }
+    }
+  }
+}
+
+// -------------------------------------------------------------- attention
+constexpr int kBQ = 64;         // query rows per CTA
+constexpr int kBK = 64;         // key rows per tile
+constexpr int kAttnThreads = 256;
+constexpr int kPad = 4;         // shared-memory row padding (floats)
+
+template <bool kFast>
+__device__ __forceinline__ float exp_mode(float v) {
+  if constexpr (kFast) {
+    return __expf(v);
+  } else {
+    return expf(v);
+  }
+}
+
+// Thread layout: ty = tid / 16 owns query rows 4*ty .. 4*ty+3 of the tile;
+// tx = tid % 16 owns key columns 4*tx .. 4*tx+3 of the score tile and output
+// columns {4*tx + 64*j .. +3} (j < DP/64).  The 16 threads of a row group are
+// 16 consecutive lanes of one warp, so row reductions are warp shuffles.
+// Shared memory (floats): Qt [DP][BQ+pad], Kt [DP][BK+pad] (both d-major),
+// V [BK][DP+pad], Pt [BK][BQ+pad].
+template <int DP, bool kFast>
+__global__ void __launch_bounds__(kAttnThreads, 1)
+    attention_kernel(const float *__restrict__ q, const float *__restrict__ k, const float *__restrict__ v,
+                     float *__restrict__ o, int64_t Lq, int64_t Lk, int D, float scale, int causal) {
+  extern __shared__ __align__(16) float sm[];
+  float *Qt = sm;
+  float *Kt = Qt + DP * (kBQ + kPad);
+  float *Vs = Kt + DP * (kBK + kPad);
+  float *Pt = Vs + kBK * (DP + kPad);
+  constexpr int kOC = DP / 64;  // output float4 groups per thread
+
+  const int tid = threadIdx.x;
+  const int ty = tid >> 4, tx = tid & 15;
+  const int64_t bh = blockIdx.y;
+  const int64_t q0 = static_cast<int64_t>(blockIdx.x) * kBQ;
+  const float *qb = q + bh * Lq * D;
+  const float *kb = k + bh * Lk * D;
+  const float *vb = v + bh * Lk * D;
+  float *ob = o + bh * Lq * D;
+
+  pdl_launch_dependents();
+  pdl_wait();
+  // Q tile, transposed: Qt[d][r] (zero past Lq / D).
+  for (int e = tid; e < kBQ * DP; e += kAttnThreads) {
+    const int r = e / DP, d = e % DP;
+    const int64_t qi = q0 + r;
+    Qt[d * (kBQ + kPad) + r] = (qi < Lq && d < D) ? qb[qi * D + d] : 0.f;
+  }
+
+  float m[4], l[4], acc[4][kOC][4];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    m[i] = -INFINITY;
+    l[i] = 0.f;
+#pragma unroll
+    for (int j = 0; j < kOC; ++j)
+#pragma unroll
+      for (int c = 0; c < 4; ++c) acc[i][j][c] = 0.f;
+  }
+
+  // With the causal mask, key tiles past the tile's last query row carry no weight.
+  int64_t k_end = Lk;
+  if (causal) {
+    const int64_t last_q = (q0 + kBQ - 1 < Lq - 1 ? q0 + kBQ - 1 : Lq - 1);
+    k_end = last_q + 1 < Lk ? last_q + 1 : Lk;
+  }
+  for (int64_t k0 = 0; k0 < k_end; k0 += kBK) {
+    __syncthreads();  // the previous tile's Kt / Vs / Pt are no longer read
+    for (int e = tid; e < kBK * DP; e += kAttnThreads) {
+      const int r = e / DP, d = e % DP;
+      const int64_t ki = k0 + r;
+      const bool in = ki < Lk && d < D;
+      Kt[d * (kBK + kPad) + r] = in ? kb[ki * D + d] : 0.f;
+      Vs[r * (DP + kPad) + d] = in ? vb[ki * D + d] : 0.f;
+    }
+    __syncthreads();
+    // S = Q K^T for this thread's 4 x 4 block, the sum over d in order.
+    float s[4][4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i)
+#pragma unroll
+      for (int j = 0; j < 4; ++j) s[i][j] = 0.f;
+#pragma unroll 4
+    for (int d = 0; d < DP; ++d) {
+      const float4 a = *reinterpret_cast<const float4 *>(&Qt[d * (kBQ + kPad) + 4 * ty]);
+      const float4 b = *reinterpret_cast<const float4 *>(&Kt[d * (kBK + kPad) + 4 * tx]);
+      const float av[4] = {a.x, a.y, a.z, a.w}, bv[4] = {b.x, b.y, b.z, b.w};
+#pragma unroll
+      for (int i = 0; i < 4; ++i)
+#pragma unroll
+        for (int j = 0; j < 4; ++j) s[i][j] = fmaf(av[i], bv[j], s[i][j]);
+    }
+    // scale, mask, running max / sum per row (16 lanes share a row group)
+    float p[4][4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const int64_t qi = q0 + 4 * ty + i;
+      float rmax = -INFINITY;
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const int64_t ki = k0 + 4 * tx + j;
+        float sv = s[i][j] * scale;
+        if (ki >= Lk || (causal && ki > qi)) sv = -INFINITY;
+        s[i][j] = sv;
+        rmax = fmaxf(rmax, sv);
+      }
+#pragma unroll
+      for (int off = 8; off >= 1; off >>= 1) rmax = fmaxf(rmax, __shfl_xor_sync(0xffffffffu, rmax, off));
+      const float m_new = fmaxf(m[i], rmax);
+      // a row with no unmasked key yet keeps m = -inf: its weights are 0
+      const float corr = (m_new == -INFINITY) ? 1.f : exp_mode<kFast>(m[i] - m_new);
+      float rsum = 0.f;
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        p[i][j] = (s[i][j] == -INFINITY) ? 0.f : exp_mode<kFast>(s[i][j] - m_new);
+        rsum += p[i][j];
+      }
+#pragma unroll
+      for (int off = 8; off >= 1; off >>= 1) rsum += __shfl_xor_sync(0xffffffffu, rsum, off);
+      l[i] = l[i] * corr + rsum;
+      m[i] = m_new;
+#pragma unroll
+      for (int jj = 0; jj < kOC; ++jj)
+#pragma unroll
+        for (int c = 0; c < 4; ++c) acc[i][jj][c] *= corr;
+    }
+    // P^T to shared memory: Pt[key][row]
+#pragma unroll
+    for (int j = 0; j < 4; ++j)
+      *reinterpret_cast<float4 *>(&Pt[(4 * tx + j) * (kBQ + kPad) + 4 * ty]) =
+          make_float4(p[0][j], p[1][j], p[2][j], p[3][j]);
+    __syncthreads();
+    // O += P V
+#pragma unroll 4
+    for (int kk = 0; kk < kBK; ++kk) {
+      const float4 pr = *reinterpret_cast<const float4 *>(&Pt[kk * (kBQ + kPad) + 4 * ty]);
+      const float pv[4] = {pr.x, pr.y, pr.z, pr.w};
+#pragma unroll
+      for (int jj = 0; jj < kOC; ++jj) {
+        const float4 vv = *reinterpret_cast<const float4 *>(&Vs[kk * (DP + kPad) + 64 * jj + 4 * tx]);
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          acc[i][jj][0] = fmaf(pv[i], vv.x, acc[i][jj][0]);
+          acc[i][jj][1] = fmaf(pv[i], vv.y, acc[i][jj][1]);
+          acc[i][jj][2] = fmaf(pv[i], vv.z, acc[i][jj][2]);
+          acc[i][jj][3] = fmaf(pv[i], vv.w, acc[i][jj][3]);
+        }
+      }
+    }
+  }
+  // O = init + acc / l
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const int64_t qi = q0 + 4 * ty + i;
+    if (qi >= Lq || l[i] == 0.f) continue;  // no key (Lk = 0): O keeps its initial value
+    const float inv = 1.f / l[i];
+#pragma unroll
+    for (int jj = 0; jj < kOC; ++jj) {
+#pragma unroll
+      for (int c = 0; c < 4; ++c) {
+        const int d = 64 * jj + 4 * tx + c;
+        if (d < D) ob[qi * D + d] += acc[i][jj][c] * inv;
+      }
+    }
+  }
+}
+
+// One warp per query row, for head dimensions above 256: scores in three
+// passes over the keys (max, sum, weighted V) -- the reference's order.
+template <bool kFast>
+__global__ void attention_rows_kernel(const float *__restrict__ q, const float *__restrict__ k,
+                                      const float *__restrict__ v, float *__restrict__ o, int64_t Lq, int64_t Lk,
+                                      int D, float scale, int causal) {
+  const int lane = threadIdx.x & 31;
+  const int64_t row = static_cast<int64_t>(blockIdx.x) * (blockDim.x / 32) + (threadIdx.x >> 5);
+  const int64_t bh = blockIdx.y;
+  pdl_launch_dependents();
+  pdl_wait();
+  if (row >= Lq) return;
+  const float *qr = q + (bh * Lq + row) * D;
+  const float *kb = k + bh * Lk * D;
+  const float *vb = v + bh * Lk * D;
+  float *orow = o + (bh * Lq + row) * D;
+  const int64_t kn = causal ? (row + 1 < Lk ? row + 1 : Lk) : Lk;
+  auto score = [&](int64_t j) {
+    float s = 0.f;
+    for (int d = lane; d < D; d += 32) s = fmaf(qr[d], kb[j * D + d], s);
+#pragma unroll
+    for (int off = 16; off >= 1; off >>= 1) s += __shfl_xor_sync(0xffffffffu, s, off);
+    return s * scale;
+  };
+  float mx = -INFINITY;
+  for (int64_t j = 0; j < kn; ++j) mx = fmaxf(mx, score(j));
+  float den = 0.f;
+  for (int64_t j = 0; j < kn; ++j) den += exp_mode<kFast>(score(j) - mx);
+  if (den == 0.f) return;  // no key (Lk = 0): O keeps its initial value
+  for (int d0 = 0; d0 < D; d0 += 32) {
+    const int d = d0 + lane;
+    float val = 0.f;
+    for (int64_t j = 0; j < kn; ++j) {
+      const float w = exp_mode<kFast>(score(j) - mx) / den;
+      if (d < D) val = fmaf(w, vb[j * D + d], val);
+    }
+    if (d < D) orow[d] += val;
+  }
+}
+
+template <int DP>
+int attention_smem_bytes() {
+  return (DP * (kBQ + kPad) + DP * (kBK + kPad) + kBK * (DP + kPad) + kBK * (kBQ + kPad)) *
+         static_cast<int>(sizeof(float));
+}
+
+template <int DP, bool kFast>
+cudaError_t launch_attention_dp(const float *q, const float *k, const float *v, float *o, int64_t BH, int64_t Lq,
+                                int64_t Lk, int D, float scale, int causal, cudaStream_t stream) {
+  auto kern = attention_kernel<DP, kFast>;
+  const int smem = attention_smem_bytes<DP>();
+  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+  if (e != cudaSuccess) return e;
+  cudaLaunchConfig_t cfg = {};
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.gridDim = dim3(static_cast<unsigned>((Lq + kBQ - 1) / kBQ), static_cast<unsigned>(BH));
+  cfg.blockDim = dim3(kAttnThreads);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  e = cudaLaunchKernelEx(&cfg, kern, q, k, v, o, Lq, Lk, D, scale, causal);
+  return e != cudaSuccess ? e : cudaGetLastError();
+}
+
+template <bool kFast>
+cudaError_t launch_attention_mode(const float *q, const float *k, const float *v, float *o, int64_t BH, int64_t Lq,
+                                  int64_t Lk, int D, float scale, int causal, cudaStream_t stream) {
+  if (D <= 64) return launch_attention_dp<64, kFast>(q, k, v, o, BH, Lq, Lk, D, scale, causal, stream);
+  if (D <= 128) return launch_attention_dp<128, kFast>(q, k, v, o, BH, Lq, Lk, D, scale, causal, stream);
+  const dim3 block(256);
+  const dim3 grid(static_cast<unsigned>((Lq + 7) / 8), static_cast<unsigned>(BH));
+  attention_rows_kernel<kFast><<<grid, block, 0, stream>>>(q, k, v, o, Lq, Lk, D, scale, causal);
+  return cudaGetLastError();
+}
+
+}  // namespace
+
+bool rope_supported(int64_t B, int64_t H, int64_t L, int64_t D) {
+  return B >= 0 && H >= 0 && L >= 0 && D >= 2 && D % 2 == 0 && D <= 8192 && L < (int64_t(1) << 31) * 64;
+}
+
+cudaError_t rope_launch(const float *x, const int64_t *pos, float *y, int64_t B, int64_t H, int64_t L, int64_t D,
+                        double theta, int fast_math, cudaStream_t stream) {
+  if (B == 0 || H == 0 || L == 0) return cudaSuccess;
+  if (!rope_supported(B, H, L, D)) return cudaErrorInvalidValue;
+  const int half = static_cast<int>(D / 2);
+  int P = kRopeTableBytes / (half * static_cast<int>(sizeof(float2)));
+  if (P > 16) P = 16;
+  if (P < 1) P = 1;
+  const int smem = P * half * static_cast<int>(sizeof(float2));
+  const int64_t blocks = (L + P - 1) / P;
+  if (blocks > INT32_MAX) return cudaErrorInvalidValue;
+  cudaLaunchConfig_t cfg = {};
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.gridDim = dim3(static_cast<unsigned>(blocks));
+  cfg.blockDim = dim3(kRopeThreads);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  cudaError_t e = fast_math ? cudaLaunchKernelEx(&cfg, rope_kernel<true>, x, pos, y, B * H, L, static_cast<int>(D), P,
+                                                 theta)
+                            : cudaLaunchKernelEx(&cfg, rope_kernel<false>, x, pos, y, B * H, L, static_cast<int>(D),
+                                                 P, theta);
+  return e != cudaSuccess ? e : cudaGetLastError();
+}
+
+bool attention_supported(int64_t B, int64_t H, int64_t Lq, int64_t Lk, int64_t D) {
+  return B >= 0 && H >= 0 && Lq >= 0 && Lk >= 0 && D >= 1 && D <= 4096 && B * H <= 65535 &&
+         (Lq + 63) / 64 <= INT32_MAX;
+}
+
+cudaError_t attention_launch(const float *q, const float *k, const float *v, float *o, int64_t B, int64_t H,
+                             int64_t Lq, int64_t Lk, int64_t D, float scale, int causal, int fast_math,
+                             cudaStream_t stream) {
+  if (B == 0 || H == 0 || Lq == 0) return cudaSuccess;
+  if (!attention_supported(B, H, Lq, Lk, D)) return cudaErrorInvalidValue;
+  return fast_math ? launch_attention_mode<true>(q, k, v, o, B * H, Lq, Lk, static_cast<int>(D), scale, causal, stream)
+                   : launch_attention_mode<false>(q, k, v, o, B * H, Lq, Lk, static_cast<int>(D), scale, causal,
+                                                  stream);
+}
+
+}  // namespace llk_b200

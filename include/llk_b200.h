@@ -145,6 +145,32 @@ void llk_swiglu_memref(MemRef2D *x, MemRef2D *wg, MemRef2D *wu, MemRef2D *init, 
 int llk_matmul(const Tensor2D *a, const Tensor2D *b, Tensor2D *c, int accumulate, KernelContext *ctx,
                const llk_gpu_context *gpu);
 
+/* ---- llk.rope / llk.attention (include/LLK/Dialect/LLKOps.td:69-131) -----
+ * The reference's other two LLK ops, lowered by
+ * lib/Conversion/LLKToLinalg/LLKToLinalg.cpp:162-615.  All arrays are
+ * contiguous row-major; f32 data, i64 position ids.  Host arrays are staged
+ * through the device and the call returns with the result on the host;
+ * device arrays must live on the call's device (asynchronous on
+ * gpu->stream).  gpu->math_mode STRICT uses accurate cos / sin / exp (the
+ * ops' math.cos / math.sin / math.exp), the fast modes the hardware's
+ * approximations. */
+
+/* RoPE: y[b,h,p,2i]   = x[..,2i] * c - x[..,2i+1] * s,
+ *       y[b,h,p,2i+1] = x[..,2i+1] * c + x[..,2i] * s,
+ * c, s = cos / sin of (f32) position_ids[p] * theta^(-2i/D) (computed in
+ * f64).  x, y: [B, H, L, D] (y may equal x); position_ids: [L]; D even
+ * (else LLK_ERR_SHAPE), theta > 0. */
+int llk_rope(const float *x, const int64_t *position_ids, float *y, int64_t B, int64_t H, int64_t L, int64_t D,
+             double theta, const llk_gpu_context *gpu);
+
+/* Attention, destination-passing like the op (its `init` operand):
+ *   o[b,h,i,:] += sum_j softmax_j(scale * q[b,h,i,:] . k[b,h,j,:]) v[b,h,j,:],
+ * with keys j > i masked out when causal.  q, o: [B, H, Lq, D]; k, v:
+ * [B, H, Lk, D]; o must not alias q, k or v (LLK_ERR_ARG).  With Lk = 0, o
+ * keeps its values.  B * H <= 65535. */
+int llk_attention(const float *q, const float *k, const float *v, float *o, int64_t B, int64_t H, int64_t Lq,
+                  int64_t Lk, int64_t D, float scale, int causal, const llk_gpu_context *gpu);
+
 /* Status of the last call on this host thread (llk_swiglu, _memref). */
 int llk_last_status(void);
 const char *llk_status_string(int status);

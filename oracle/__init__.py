@@ -11,7 +11,10 @@ It wraps ``_build/liboracle.so`` built from:
     ``lib/Transforms/FuseDoubleContraction.cpp:119-199``), bit-exact against
     the reference compiled from its own sources (``_ref/ref_driver``);
   * ``swiglu_port.c`` -- threaded fused-schedule restatement used as the CPU
-    baseline (``lib/Transforms/TileAndVectorize.cpp:53-57`` tiling).
+    baseline (``lib/Transforms/TileAndVectorize.cpp:53-57`` tiling);
+  * ``rope_attention_oracle.c`` -- the llk.rope / llk.attention lowerings
+    (``lib/Conversion/LLKToLinalg/LLKToLinalg.cpp:162-608``) in f32 and the
+    reference tests' FP64 references.
 """
 from __future__ import annotations
 
@@ -54,6 +57,10 @@ def lib():
         L.oracle_bf16_to_f32_array.argtypes = [p, p, i64]
         L.port_swiglu.argtypes = [p, i64, p, p, i64, i64, i64, i64, p, p, i64, i32]
         L.port_matmul.argtypes = [p, i64, p, i64, p, i64, i64, i64, i64, i32]
+        L.oracle_rope_f32.argtypes = [p, p, p, i64, i64, i64, i64, ctypes.c_double]
+        L.oracle_rope_fp64.argtypes = [p, p, p, i64, i64, i64, i64, ctypes.c_double]
+        L.oracle_attention_f32.argtypes = [p, p, p, p, i64, i64, i64, i64, i64, ctypes.c_float, i32]
+        L.oracle_attention_fp64.argtypes = [p, p, p, p, i64, i64, i64, i64, i64, ctypes.c_double, i32]
         _lib = L
     return _lib
 
@@ -187,3 +194,43 @@ def classify_m(M: int) -> int:
 
 def ref_driver_available() -> bool:
     return os.path.exists(REF_DRIVER)
+
+
+def rope_f32(x, pos, theta: float = 10000.0) -> np.ndarray:
+    """llk.rope as lowered by the reference (f32 result)."""
+    x = _c(x, np.float32)
+    pos = _c(pos, np.int64)
+    B, H, L, D = x.shape
+    y = np.empty_like(x)
+    lib().oracle_rope_f32(_ptr(x), _ptr(pos), _ptr(y), B, H, L, D, float(theta))
+    return y
+
+
+def rope_fp64(x, pos, theta: float = 10000.0) -> np.ndarray:
+    """FP64 RoPE of the reference's tests (rope_correctness.cpp:14-35)."""
+    x = _c(x, np.float64)
+    pos = _c(pos, np.int64)
+    B, H, L, D = x.shape
+    y = np.empty_like(x)
+    lib().oracle_rope_fp64(_ptr(x), _ptr(pos), _ptr(y), B, H, L, D, float(theta))
+    return y
+
+
+def attention_f32(q, k, v, scale: float, causal: bool, init=None) -> np.ndarray:
+    """llk.attention as lowered by the reference: init + softmax(scale QK^T) V (f32)."""
+    q, k, v = _c(q, np.float32), _c(k, np.float32), _c(v, np.float32)
+    B, H, Lq, D = q.shape
+    Lk = k.shape[2]
+    o = np.zeros_like(q) if init is None else _c(init, np.float32).copy()
+    lib().oracle_attention_f32(_ptr(q), _ptr(k), _ptr(v), _ptr(o), B, H, Lq, Lk, D, float(scale), int(bool(causal)))
+    return o
+
+
+def attention_fp64(q, k, v, scale: float, causal: bool) -> np.ndarray:
+    """FP64 attention of the reference's tests (attention_correctness.cpp:15-60)."""
+    q, k, v = _c(q, np.float64), _c(k, np.float64), _c(v, np.float64)
+    B, H, Lq, D = q.shape
+    Lk = k.shape[2]
+    o = np.zeros_like(q)
+    lib().oracle_attention_fp64(_ptr(q), _ptr(k), _ptr(v), _ptr(o), B, H, Lq, Lk, D, float(scale), int(bool(causal)))
+    return o
