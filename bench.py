@@ -541,11 +541,7 @@ def our_arm(args):
                     cpu["reference_naive"] = naive
 
     # every parity figure of the run, headline and secondary, in one place
-    for key in ("gather_y", "fused_allgather"):
-        if isinstance(extras.get(key), dict) and "parity" in extras[key]:
-            parity[key] = extras[key]["parity"]
-    for key, sub in (("decode_c4", None), ("swiglu_c5", None)):
-        v = extras.get(key)
+    for key, v in extras.items():
         if isinstance(v, dict):
             if "parity" in v:
                 parity[key] = v["parity"]
@@ -557,6 +553,8 @@ def our_arm(args):
         expected += ["gather_y", "fused_allgather"]
     if not args.quick:
         expected += ["decode_c4.c4_m1", "decode_c4.c4_m4", "decode_c4.c4_m16", "swiglu_c5"]
+        if world == 1:
+            expected += ["matmul_c2", "rope", "attention"]
     missing = [k for k in expected if k not in parity]
     worst = max((p["max_rel_err"] for p in parity.values()), default=float("inf"))
     parity_line = {"max_rel_err": worst, "tol": TOL_BF16, "ok": bool(worst <= TOL_BF16 and not missing),
@@ -799,6 +797,93 @@ def single_gpu_extras(args, dev, stream, peaks, headline_tflops):
                         "what": "torch.mm X[2048,4096] x [Wg|Wu][4096,22016] bf16 -> bf16 (same FLOPs, no SiLU "
                                 "epilogue), same rotation and timing as the headline, measured right after it"}
     del X, W
+    torch.cuda.empty_cache()
+    out.update(rope_attention_extras(args, dev, stream, peaks))
+    return out
+
+
+def rope_attention_extras(args, dev, stream, peaks):
+    """The reference's other two LLK ops at Llama-7B attention shapes (32
+    heads of 128, f32 as the ops are): RoPE over [1, 32, 4096, 128]
+    (HBM-bound: read x, write y) and causal attention over [1, 32, 2048, 128]
+    (FLOP-bound on the CUDA cores: the op is f32).  Same rotation / timing
+    rules as the headline; parity at sampled rows against the CPU oracle."""
+    import torch
+
+    import dslcompiler_b200 as llk
+    import oracle
+
+    out = {}
+    steps = max(5, min(args.steps, 100))
+    l2 = torch.cuda.get_device_properties(dev).L2_cache_size
+    g = torch.Generator(device=dev).manual_seed(9)
+    B, H, L, D = 1, 32, 4096, 128
+    x = torch.randn((B, H, L, D), generator=g, device=dev)
+    pos = torch.arange(L, device=dev, dtype=torch.int64)
+    y = torch.empty_like(x)
+    sets, _ = input_sets(dev, [x, y], l2)
+
+    def rope_step(i):
+        a, b_ = sets[i % len(sets)]
+        llk.rope(a, pos, out=b_)
+
+    for i in range(3):
+        rope_step(i)
+    ms_eager = time_back_to_back(rope_step, steps, stream) / steps
+    # the same launches replayed from one CUDA graph: the GPU time without
+    # the host's per-call cost (about the kernel time at this size)
+    graph = torch.cuda.CUDAGraph()
+    side = torch.cuda.Stream(dev)
+    side.wait_stream(stream)
+    with torch.cuda.stream(side):
+        with torch.cuda.graph(graph, stream=side, capture_error_mode="thread_local"):
+            for i in range(steps):
+                rope_step(i)
+    torch.cuda.synchronize()
+    graph.replay()
+    torch.cuda.synchronize()
+    ms = time_back_to_back(lambda i: graph.replay(), 3, stream) / (3 * steps)
+    del graph
+    byts = 2 * x.numel() * 4 + L * 8
+    hs = [0, 17, 31]
+    ref = oracle.rope_f32(x[:, hs].cpu().numpy(), pos.cpu().numpy(), 10000.0)
+    err = float(np.abs(sets[0][1][:, hs].cpu().numpy() - ref).max() / np.abs(ref).max())
+    out["rope"] = {"shape": [B, H, L, D], "us": ms * 1e3, "us_eager": ms_eager * 1e3,
+                   "timing": "us: back-to-back calls replayed from one CUDA graph; us_eager: issued from Python",
+                   "GB/s": byts / (ms * 1e-3) / 1e9,
+                   "frac_of_hbm": byts / (ms * 1e-3) / 1e9 / peaks["hbm"], "parity": {"max_rel_err": err},
+                   "what": "llk_rope, f32 [1,32,4096,128], positions 0..4095, theta 1e4, strict cos/sin"}
+    del sets, x, y
+    Lq = 2048
+    q = torch.randn((B, H, Lq, D), generator=g, device=dev)
+    k = torch.randn((B, H, Lq, D), generator=g, device=dev)
+    v = torch.randn((B, H, Lq, D), generator=g, device=dev)
+    o = torch.zeros_like(q)
+    asteps = max(3, min(args.steps, 10))
+
+    def attn_step(i):
+        llk.attention(q, k, v, causal=True, out=o)
+
+    attn_step(0)
+    ams = time_back_to_back(attn_step, asteps, stream) / asteps
+    flops = 4.0 * B * H * Lq * Lq * D / 2  # causal: half the score matrix
+    o.zero_()
+    attn_step(0)
+    torch.cuda.synchronize()
+    hs = [0, 31]
+    ref = oracle.attention_f32(q[:, hs].cpu().numpy(), k[:, hs].cpu().numpy(), v[:, hs].cpu().numpy(),
+                               1.0 / np.sqrt(D), True)
+    err = float(np.abs(o[:, hs].cpu().numpy() - ref).max() / np.abs(ref).max())
+    sm_clock_ghz = 1.965
+    f32_peak = 148 * 128 * 2 * sm_clock_ghz * 1e9 / 1e12
+    out["attention"] = {"shape": [B, H, Lq, Lq, D], "causal": True, "ms": ams,
+                        "tflops": flops / (ams * 1e-3) / 1e12,
+                        "frac_of_f32_fma_peak": flops / (ams * 1e-3) / 1e12 / f32_peak,
+                        "f32_fma_peak_tflops": f32_peak, "parity": {"max_rel_err": err},
+                        "what": "llk_attention f32 on the CUDA cores; peak = 148 SMs x 128 FMA lanes x 2 x 1.965 GHz "
+                                "(nominal, not measured)"}
+    llk.synchronize(dev.index)
+    del q, k, v, o
     torch.cuda.empty_cache()
     return out
 

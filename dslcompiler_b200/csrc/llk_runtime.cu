@@ -938,7 +938,7 @@ struct FlatArg {
 };
 
 int run_flat(const llk_gpu_context *gpu, FlatArg *args, int nargs,
-             const std::function<cudaError_t(void **, cudaStream_t, bool)> &launch) {
+             const std::function<cudaError_t(void **, cudaStream_t, bool, DeviceState &)> &launch) {
   DeviceRestore restore;
   if (gpu && (gpu->math_mode < LLK_MATH_STRICT || gpu->math_mode > LLK_MATH_UNSAFE_FAST)) return LLK_ERR_ARG;
   int dev, rc;
@@ -962,7 +962,9 @@ int run_flat(const llk_gpu_context *gpu, FlatArg *args, int nargs,
     ptrs[i] = const_cast<void *>(st[i].t.data);
     any_host = any_host || st[i].host;
   }
-  if (launch(ptrs, stream, fast) != cudaSuccess) return LLK_ERR_CUDA;
+  const cudaError_t le = launch(ptrs, stream, fast, *ds);
+  if (le == cudaErrorMemoryAllocation) return LLK_ERR_NOMEM;
+  if (le != cudaSuccess) return LLK_ERR_CUDA;
   for (int i = 0; i < nargs; ++i)
     if (args[i].out && (rc = stage_out(st[i], args[i].elem, stream)) != LLK_OK) return rc;
   if (any_host) return read_and_clear_status(*ds, stream);
@@ -978,18 +980,32 @@ int llk_rope(const float *x, const int64_t *position_ids, float *y, int64_t B, i
   const int64_t n = B * H * L * D;
   if (n == 0) return LLK_OK;
   if (!(theta > 0.0)) return LLK_ERR_ARG;
-  FlatArg a[3] = {{x, n, 4, false, true}, {position_ids, L, 8, false, true}, {y, n, 4, true, x == y}};
+  // The (cos, sin) table goes to the partial-sum region of the device
+  // workspace (written before it is read; calls on one device are serialised).
+  auto table = [&](DeviceState &ds, void **out) {
+    if (ds.workspace.ensure(kWsPartials + rope_table_bytes(L, D), true) != cudaSuccess)
+      return cudaErrorMemoryAllocation;
+    *out = static_cast<char *>(ds.workspace.ptr) + kWsPartials;
+    return cudaSuccess;
+  };
   if (x == y) {
     // in place: one buffer, read and written
     FlatArg b[2] = {{x, n, 4, true, true}, {position_ids, L, 8, false, true}};
-    return run_flat(gpu, b, 2, [&](void **p, cudaStream_t s, bool fast) {
+    return run_flat(gpu, b, 2, [&](void **p, cudaStream_t s, bool fast, DeviceState &ds) {
+      void *tab = nullptr;
+      const cudaError_t e = table(ds, &tab);
+      if (e != cudaSuccess) return e;
       return rope_launch(static_cast<float *>(p[0]), static_cast<const int64_t *>(p[1]), static_cast<float *>(p[0]),
-                         B, H, L, D, theta, fast ? 1 : 0, s);
+                         B, H, L, D, theta, fast ? 1 : 0, tab, ds.sm_count, s);
     });
   }
-  return run_flat(gpu, a, 3, [&](void **p, cudaStream_t s, bool fast) {
+  FlatArg a[3] = {{x, n, 4, false, true}, {position_ids, L, 8, false, true}, {y, n, 4, true, false}};
+  return run_flat(gpu, a, 3, [&](void **p, cudaStream_t s, bool fast, DeviceState &ds) {
+    void *tab = nullptr;
+    const cudaError_t e = table(ds, &tab);
+    if (e != cudaSuccess) return e;
     return rope_launch(static_cast<const float *>(p[0]), static_cast<const int64_t *>(p[1]), static_cast<float *>(p[2]),
-                       B, H, L, D, theta, fast ? 1 : 0, s);
+                       B, H, L, D, theta, fast ? 1 : 0, tab, ds.sm_count, s);
   });
 }
 
@@ -1001,7 +1017,7 @@ int llk_attention(const float *q, const float *k, const float *v, float *o, int6
   if (o == q || o == k || o == v) return LLK_ERR_ARG;  // O accumulates while Q, K, V are read
   const int64_t nq = B * H * Lq * D, nk = B * H * Lk * D;
   FlatArg a[4] = {{q, nq, 4, false, true}, {k, nk, 4, false, true}, {v, nk, 4, false, true}, {o, nq, 4, true, true}};
-  return run_flat(gpu, a, 4, [&](void **p, cudaStream_t s, bool fast) {
+  return run_flat(gpu, a, 4, [&](void **p, cudaStream_t s, bool fast, DeviceState &) {
     return attention_launch(static_cast<const float *>(p[0]), static_cast<const float *>(p[1]),
                             static_cast<const float *>(p[2]), static_cast<float *>(p[3]), B, H, Lq, Lk, D, scale,
                             causal ? 1 : 0, fast ? 1 : 0, s);

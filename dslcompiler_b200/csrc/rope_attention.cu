@@ -9,9 +9,9 @@
 //   c, s = cos / sin of the angle rounded to f32,
 //   y[2i] = x[2i]*c - x[2i+1]*s,  y[2i+1] = x[2i+1]*c + x[2i]*s  (f32, each
 //   product and sum rounded on its own, as the unfused arith ops are).
-// HBM-bound: a CTA takes a block of positions, builds their cos/sin table in
-// shared memory once, then streams those positions' rows of every (b, h)
-// with 16-byte loads and stores.
+// HBM-bound: a small kernel builds the (cos, sin) table [L][D/2] once per
+// call (it stays in L2), then a grid-stride kernel streams x -> y with
+// 16-byte loads and stores, several in flight per thread.
 //
 // Attention (q [B,H,Lq,D], k/v [B,H,Lk,D] f32, scale, causal):
 //   O = init + softmax(scale * Q K^T, masked where k > q when causal) V.
@@ -36,7 +36,6 @@ namespace {
 
 // ------------------------------------------------------------------- RoPE
 constexpr int kRopeThreads = 256;
-constexpr int kRopeTableBytes = 48 * 1024;
 
 template <bool kFast>
 __device__ __forceinline__ void sincos_mode(float a, float *s, float *c) {
@@ -54,57 +53,77 @@ __device__ __forceinline__ float2 rotate(float e, float o, float c, float s) {
   return make_float2(__fsub_rn(__fmul_rn(e, c), __fmul_rn(o, s)), __fadd_rn(__fmul_rn(o, c), __fmul_rn(e, s)));
 }
 
-// Grid: one CTA per block of P positions.  Shared memory: the block's
-// (cos, sin) table [P][D/2] as float2.
+// The (cos, sin) table [L][D/2] (float2), built once per call: the
+// frequencies and angles in f64, the trig of the f32 angle.
 template <bool kFast>
-__global__ void __launch_bounds__(kRopeThreads) rope_kernel(const float *__restrict__ x,
-                                                           const int64_t *__restrict__ pos, float *__restrict__ y,
-                                                           int64_t BH, int64_t L, int D, int P, double theta) {
-  extern __shared__ float2 table[];
+__global__ void __launch_bounds__(kRopeThreads) rope_table_kernel(const int64_t *__restrict__ pos,
+                                                                 float2 *__restrict__ table, int64_t L, int D,
+                                                                 double theta) {
   const int half = D / 2;
-  const int64_t p0 = static_cast<int64_t>(blockIdx.x) * P;
-  const int np = static_cast<int>(L - p0 < P ? L - p0 : P);
   pdl_launch_dependents();
   pdl_wait();
-  for (int e = threadIdx.x; e < np * half; e += blockDim.x) {
-    const int pi = e / half, i = e % half;
+  for (int64_t e = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; e < L * half;
+       e += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const int64_t p = e / half;
+    const int i = static_cast<int>(e % half);
     const double freq = pow(theta, (-2.0 * static_cast<double>(i)) / static_cast<double>(D));
-    const double angle = static_cast<double>(pos[p0 + pi]) * freq;
+    const double angle = static_cast<double>(pos[p]) * freq;
     float s, c;
     sincos_mode<kFast>(static_cast<float>(angle), &s, &c);
     table[e] = make_float2(c, s);
   }
-  __syncthreads();
-  // The block's rows of one (b, h) are np * D contiguous floats.
-  const int64_t row_elems = static_cast<int64_t>(np) * D;
-  if ((D & 3) == 0) {
-    const int n4 = static_cast<int>(row_elems / 4);
-    for (int64_t bh = 0; bh < BH; ++bh) {
-      const int64_t base = (bh * L + p0) * D;
-      const float4 *src = reinterpret_cast<const float4 *>(x + base);
-      float4 *dst = reinterpret_cast<float4 *>(y + base);
-      for (int v = threadIdx.x; v < n4; v += blockDim.x) {
-        const float4 a = __ldcs(src + v);
-        const int e = v * 4;                   // element in the block
-        const int pi = e / D, i = (e % D) / 2;  // pair index of a.x, a.y
-        const float2 cs0 = table[pi * half + i], cs1 = table[pi * half + i + 1];
-        const float2 r0 = rotate(a.x, a.y, cs0.x, cs0.y), r1 = rotate(a.z, a.w, cs1.x, cs1.y);
-        __stcs(dst + v, make_float4(r0.x, r0.y, r1.x, r1.y));
+}
+
+// Streams x -> y with 16-byte accesses (D % 4 == 0; two pairs per access,
+// their (cos, sin) one 16-byte table load from L2), kUnroll accesses in
+// flight per thread; grid-stride over the whole tensor.
+constexpr int kUnroll = 4;
+__global__ void __launch_bounds__(kRopeThreads) rope_apply4_kernel(const float4 *__restrict__ x,
+                                                                  const float4 *__restrict__ table,
+                                                                  float4 *__restrict__ y, int64_t n4, int64_t L,
+                                                                  int D) {
+  pdl_launch_dependents();
+  pdl_wait();
+  const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
+  const int q4 = D / 4;  // accesses per row
+  for (int64_t v0 = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; v0 < n4; v0 += kUnroll * stride) {
+    float4 a[kUnroll], cs[kUnroll];
+#pragma unroll
+    for (int u = 0; u < kUnroll; ++u) {
+      const int64_t v = v0 + u * stride;
+      if (v < n4) {
+        a[u] = __ldcs(x + v);
+        const int64_t row = v / q4;  // (b, h, p) row
+        const int64_t p = row % L;
+        cs[u] = table[p * q4 + (v - row * q4)];  // pairs 2j, 2j+1 of the row: (c0, s0, c1, s1)
       }
     }
-  } else {
-    const int n2 = static_cast<int>(row_elems / 2);
-    for (int64_t bh = 0; bh < BH; ++bh) {
-      const int64_t base = (bh * L + p0) * D;
-      const float2 *src = reinterpret_cast<const float2 *>(x + base);
-      float2 *dst = reinterpret_cast<float2 *>(y + base);
-      for (int v = threadIdx.x; v < n2; v += blockDim.x) {
-        const float2 a = src[v];
-        const int pi = (v * 2) / D, i = ((v * 2) % D) / 2;
-        const float2 cs = table[pi * half + i];
-        dst[v] = rotate(a.x, a.y, cs.x, cs.y);
+#pragma unroll
+    for (int u = 0; u < kUnroll; ++u) {
+      const int64_t v = v0 + u * stride;
+      if (v < n4) {
+        const float2 r0 = rotate(a[u].x, a[u].y, cs[u].x, cs[u].y), r1 = rotate(a[u].z, a[u].w, cs[u].z, cs[u].w);
+        __stcs(y + v, make_float4(r0.x, r0.y, r1.x, r1.y));
       }
     }
+  }
+}
+
+// D % 4 == 2: one pair per 8-byte access.
+__global__ void __launch_bounds__(kRopeThreads) rope_apply2_kernel(const float2 *__restrict__ x,
+                                                                  const float2 *__restrict__ table,
+                                                                  float2 *__restrict__ y, int64_t n2, int64_t L,
+                                                                  int D) {
+  pdl_launch_dependents();
+  pdl_wait();
+  const int half = D / 2;
+  for (int64_t v = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; v < n2;
+       v += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const int64_t row = v / half;
+    const int64_t p = row % L;
+    const float2 cs = table[p * half + (v - row * half)];
+    const float2 a = x[v];
+    y[v] = rotate(a.x, a.y, cs.x, cs.y);
   }
 }
 
@@ -357,34 +376,48 @@ cudaError_t launch_attention_mode(const float *q, const float *k, const float *v
 }  // namespace
 
 bool rope_supported(int64_t B, int64_t H, int64_t L, int64_t D) {
-  return B >= 0 && H >= 0 && L >= 0 && D >= 2 && D % 2 == 0 && D <= 8192 && L < (int64_t(1) << 31) * 64;
+  return B >= 0 && H >= 0 && L >= 0 && D >= 2 && D % 2 == 0 && D <= (int64_t(1) << 20);
 }
 
+size_t rope_table_bytes(int64_t L, int64_t D) { return static_cast<size_t>(L) * static_cast<size_t>(D / 2) * 8; }
+
 cudaError_t rope_launch(const float *x, const int64_t *pos, float *y, int64_t B, int64_t H, int64_t L, int64_t D,
-                        double theta, int fast_math, cudaStream_t stream) {
+                        double theta, int fast_math, void *table, int sm_count, cudaStream_t stream) {
   if (B == 0 || H == 0 || L == 0) return cudaSuccess;
   if (!rope_supported(B, H, L, D)) return cudaErrorInvalidValue;
-  const int half = static_cast<int>(D / 2);
-  int P = kRopeTableBytes / (half * static_cast<int>(sizeof(float2)));
-  if (P > 16) P = 16;
-  if (P < 1) P = 1;
-  const int smem = P * half * static_cast<int>(sizeof(float2));
-  const int64_t blocks = (L + P - 1) / P;
-  if (blocks > INT32_MAX) return cudaErrorInvalidValue;
   cudaLaunchConfig_t cfg = {};
   cudaLaunchAttribute attr[1];
   attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
   attr[0].val.programmaticStreamSerializationAllowed = 1;
-  cfg.gridDim = dim3(static_cast<unsigned>(blocks));
   cfg.blockDim = dim3(kRopeThreads);
-  cfg.dynamicSmemBytes = smem;
   cfg.stream = stream;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  cudaError_t e = fast_math ? cudaLaunchKernelEx(&cfg, rope_kernel<true>, x, pos, y, B * H, L, static_cast<int>(D), P,
-                                                 theta)
-                            : cudaLaunchKernelEx(&cfg, rope_kernel<false>, x, pos, y, B * H, L, static_cast<int>(D),
-                                                 P, theta);
+  const int64_t pairs = L * (D / 2);
+  int64_t tb = (pairs + kRopeThreads - 1) / kRopeThreads;
+  cfg.gridDim = dim3(static_cast<unsigned>(tb < 4 * sm_count ? tb : 4 * sm_count));
+  float2 *tab = static_cast<float2 *>(table);
+  cudaError_t e = fast_math ? cudaLaunchKernelEx(&cfg, rope_table_kernel<true>, pos, tab, L, static_cast<int>(D), theta)
+                            : cudaLaunchKernelEx(&cfg, rope_table_kernel<false>, pos, tab, L, static_cast<int>(D),
+                                                 theta);
+  if (e != cudaSuccess) return e;
+  // Streaming: 8 CTAs of 256 threads per SM, grid-stride.
+  const int64_t n = B * H * L * D;
+  if ((D & 3) == 0) {
+    const int64_t n4 = n / 4;
+    const int64_t need = (n4 + kRopeThreads * kUnroll - 1) / (kRopeThreads * kUnroll);
+    cfg.gridDim = dim3(static_cast<unsigned>(need < 8 * sm_count ? need : 8 * sm_count));
+    e = cudaLaunchKernelEx(&cfg, rope_apply4_kernel, reinterpret_cast<const float4 *>(x),
+                           reinterpret_cast<const float4 *>(table), reinterpret_cast<float4 *>(y), n4, L,
+                           static_cast<int>(D));
+  } else {
+    const int64_t n2 = n / 2;
+    const int64_t need = (n2 + kRopeThreads - 1) / kRopeThreads;
+    cfg.gridDim = dim3(static_cast<unsigned>(need < 8 * sm_count ? need : 8 * sm_count));
+    e = cudaLaunchKernelEx(&cfg, rope_apply2_kernel, reinterpret_cast<const float2 *>(x),
+                           reinterpret_cast<const float2 *>(table), reinterpret_cast<float2 *>(y), n2, L,
+                           static_cast<int>(D));
+  }
   return e != cudaSuccess ? e : cudaGetLastError();
 }
 

@@ -159,7 +159,10 @@ int llk_matmul(const Tensor2D *a, const Tensor2D *b, Tensor2D *c, int accumulate
  *       y[b,h,p,2i+1] = x[..,2i+1] * c + x[..,2i] * s,
  * c, s = cos / sin of (f32) position_ids[p] * theta^(-2i/D) (computed in
  * f64).  x, y: [B, H, L, D] (y may equal x); position_ids: [L]; D even
- * (else LLK_ERR_SHAPE), theta > 0. */
+ * (else LLK_ERR_SHAPE), theta > 0.  The (cos, sin) table, L * D/2 * 8
+ * bytes, is built in the library's per-device workspace (grown with
+ * cudaMalloc on first use; calls on one device are serialised as for the
+ * other workspace users, see KernelContext). */
 int llk_rope(const float *x, const int64_t *position_ids, float *y, int64_t B, int64_t H, int64_t L, int64_t D,
              double theta, const llk_gpu_context *gpu);
 
