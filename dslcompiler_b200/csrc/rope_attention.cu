@@ -335,6 +335,195 @@ __global__ void attention_rows_kernel(const float *__restrict__ q, const float *
   }
 }
 
+// ---- double-buffered variant (D % 4 == 0): Q, K, V tiles row-major in
+// shared memory, K / V tiles copied with cp.async 16-byte chunks two tiles
+// ahead of use, so the next key tile streams in while this one computes.
+// Thread layout as above, except that thread tx owns key columns tx + 16 j
+// (j < 4): consecutive lanes read consecutive K rows, conflict-free.
+__device__ __forceinline__ void cp_async16(float *smem_dst, const float *gsrc, bool in) {
+  const uint32_t d = smem_u32(smem_dst);
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(d), "l"(gsrc), "r"(in ? 16 : 0) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait() {
+  asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
+}
+
+template <int DP, bool kFast>
+__global__ void __launch_bounds__(kAttnThreads, 1)
+    attention_db_kernel(const float *__restrict__ q, const float *__restrict__ k, const float *__restrict__ v,
+                        float *__restrict__ o, int64_t Lq, int64_t Lk, int D, float scale, int causal) {
+  extern __shared__ __align__(16) float sm[];
+  constexpr int kLd = DP + kPad;  // row stride of Q / K / V tiles
+  float *Qs = sm;                              // [BQ][kLd]
+  float *KV = Qs + kBQ * kLd;                  // 2 stages x ([BK][kLd] K, [BK][kLd] V)
+  float *Pt = KV + 2 * 2 * kBK * kLd;          // [BK][BQ+pad]
+  constexpr int kOC = DP / 64;
+  constexpr int kChunks = DP / 4;              // 16-byte chunks per row
+
+  const int tid = threadIdx.x;
+  const int ty = tid >> 4, tx = tid & 15;
+  const int64_t bh = blockIdx.y;
+  const int64_t q0 = static_cast<int64_t>(blockIdx.x) * kBQ;
+  const float *qb = q + bh * Lq * D;
+  const float *kb = k + bh * Lk * D;
+  const float *vb = v + bh * Lk * D;
+  float *ob = o + bh * Lq * D;
+
+  int64_t k_end = Lk;
+  if (causal) {
+    const int64_t last_q = (q0 + kBQ - 1 < Lq - 1 ? q0 + kBQ - 1 : Lq - 1);
+    k_end = last_q + 1 < Lk ? last_q + 1 : Lk;
+  }
+  const int n_tiles = static_cast<int>((k_end + kBK - 1) / kBK);
+
+  // chunk (row, c) of a tile: rows past the end / chunks past D read as zero
+  auto load_rows = [&](float *dst, const float *src, int64_t row0, int64_t nrows) {
+    for (int e = tid; e < kBK * kChunks; e += kAttnThreads) {
+      const int r = e / kChunks, c = e % kChunks;
+      const bool in = row0 + r < nrows && 4 * c < D;
+      const float *g = in ? src + (row0 + r) * D + 4 * c : src;
+      cp_async16(dst + r * kLd + 4 * c, g, in);
+    }
+  };
+  auto load_tile = [&](int t) {
+    float *Ks = KV + (t & 1) * 2 * kBK * kLd;
+    load_rows(Ks, kb, static_cast<int64_t>(t) * kBK, Lk);
+    load_rows(Ks + kBK * kLd, vb, static_cast<int64_t>(t) * kBK, Lk);
+  };
+
+  pdl_launch_dependents();
+  pdl_wait();
+  load_rows(Qs, qb, q0, Lq);
+  if (n_tiles > 0) load_tile(0);
+  cp_async_commit();
+
+  float m[4], l[4], acc[4][kOC][4];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    m[i] = -INFINITY;
+    l[i] = 0.f;
+#pragma unroll
+    for (int j = 0; j < kOC; ++j)
+#pragma unroll
+      for (int c = 0; c < 4; ++c) acc[i][j][c] = 0.f;
+  }
+
+  for (int t = 0; t < n_tiles; ++t) {
+    // issue tile t+1 (its buffer was last read by tile t-1, finished at the
+    // barrier that ended iteration t-1), then wait for tile t
+    if (t + 1 < n_tiles) load_tile(t + 1);
+    cp_async_commit();
+    cp_async_wait<1>();
+    __syncthreads();
+    const float *Ks = KV + (t & 1) * 2 * kBK * kLd;
+    const float *Vs = Ks + kBK * kLd;
+    const int64_t k0 = static_cast<int64_t>(t) * kBK;
+    float s[4][4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i)
+#pragma unroll
+      for (int j = 0; j < 4; ++j) s[i][j] = 0.f;
+#pragma unroll 2
+    for (int d = 0; d < DP; d += 4) {
+      float4 a[4], b[4];
+#pragma unroll
+      for (int i = 0; i < 4; ++i) a[i] = *reinterpret_cast<const float4 *>(&Qs[(4 * ty + i) * kLd + d]);
+#pragma unroll
+      for (int j = 0; j < 4; ++j) b[j] = *reinterpret_cast<const float4 *>(&Ks[(tx + 16 * j) * kLd + d]);
+#pragma unroll
+      for (int i = 0; i < 4; ++i)
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          s[i][j] = fmaf(a[i].x, b[j].x, s[i][j]);
+          s[i][j] = fmaf(a[i].y, b[j].y, s[i][j]);
+          s[i][j] = fmaf(a[i].z, b[j].z, s[i][j]);
+          s[i][j] = fmaf(a[i].w, b[j].w, s[i][j]);
+        }
+    }
+    float p[4][4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const int64_t qi = q0 + 4 * ty + i;
+      float rmax = -INFINITY;
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const int64_t ki = k0 + tx + 16 * j;
+        float sv = s[i][j] * scale;
+        if (ki >= Lk || (causal && ki > qi)) sv = -INFINITY;
+        s[i][j] = sv;
+        rmax = fmaxf(rmax, sv);
+      }
+#pragma unroll
+      for (int off = 8; off >= 1; off >>= 1) rmax = fmaxf(rmax, __shfl_xor_sync(0xffffffffu, rmax, off));
+      const float m_new = fmaxf(m[i], rmax);
+      const float corr = (m_new == -INFINITY) ? 1.f : exp_mode<kFast>(m[i] - m_new);
+      float rsum = 0.f;
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        p[i][j] = (s[i][j] == -INFINITY) ? 0.f : exp_mode<kFast>(s[i][j] - m_new);
+        rsum += p[i][j];
+      }
+#pragma unroll
+      for (int off = 8; off >= 1; off >>= 1) rsum += __shfl_xor_sync(0xffffffffu, rsum, off);
+      l[i] = l[i] * corr + rsum;
+      m[i] = m_new;
+#pragma unroll
+      for (int jj = 0; jj < kOC; ++jj)
+#pragma unroll
+        for (int c = 0; c < 4; ++c) acc[i][jj][c] *= corr;
+    }
+#pragma unroll
+    for (int j = 0; j < 4; ++j)
+      *reinterpret_cast<float4 *>(&Pt[(tx + 16 * j) * (kBQ + kPad) + 4 * ty]) =
+          make_float4(p[0][j], p[1][j], p[2][j], p[3][j]);
+    __syncthreads();
+#pragma unroll 4
+    for (int kk = 0; kk < kBK; ++kk) {
+      const float4 pr = *reinterpret_cast<const float4 *>(&Pt[kk * (kBQ + kPad) + 4 * ty]);
+      const float pv[4] = {pr.x, pr.y, pr.z, pr.w};
+#pragma unroll
+      for (int jj = 0; jj < kOC; ++jj) {
+        const float4 vv = *reinterpret_cast<const float4 *>(&Vs[kk * kLd + 64 * jj + 4 * tx]);
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          acc[i][jj][0] = fmaf(pv[i], vv.x, acc[i][jj][0]);
+          acc[i][jj][1] = fmaf(pv[i], vv.y, acc[i][jj][1]);
+          acc[i][jj][2] = fmaf(pv[i], vv.z, acc[i][jj][2]);
+          acc[i][jj][3] = fmaf(pv[i], vv.w, acc[i][jj][3]);
+        }
+      }
+    }
+    __syncthreads();  // Pt and this stage's K / V are free for the next loads
+  }
+  cp_async_wait<0>();
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const int64_t qi = q0 + 4 * ty + i;
+    if (qi >= Lq || l[i] == 0.f) continue;  // no key (Lk = 0): O keeps its initial value
+    const float inv = 1.f / l[i];
+#pragma unroll
+    for (int jj = 0; jj < kOC; ++jj) {
+      const int d = 64 * jj + 4 * tx;
+      if (d < D) {
+        float4 *dst = reinterpret_cast<float4 *>(ob + qi * D + d);
+        float4 cur = *dst;
+        cur.x += acc[i][jj][0] * inv;
+        cur.y += acc[i][jj][1] * inv;
+        cur.z += acc[i][jj][2] * inv;
+        cur.w += acc[i][jj][3] * inv;
+        *dst = cur;
+      }
+    }
+  }
+}
+
+template <int DP>
+int attention_db_smem_bytes() {
+  return ((kBQ + 4 * kBK) * (DP + kPad) + kBK * (kBQ + kPad)) * static_cast<int>(sizeof(float));
+}
+
 template <int DP>
 int attention_smem_bytes() {
   return (DP * (kBQ + kPad) + DP * (kBK + kPad) + kBK * (DP + kPad) + kBK * (kBQ + kPad)) *
@@ -344,8 +533,13 @@ int attention_smem_bytes() {
 template <int DP, bool kFast>
 cudaError_t launch_attention_dp(const float *q, const float *k, const float *v, float *o, int64_t BH, int64_t Lq,
                                 int64_t Lk, int D, float scale, int causal, cudaStream_t stream) {
-  auto kern = attention_kernel<DP, kFast>;
-  const int smem = attention_smem_bytes<DP>();
+  // rows of 16-byte chunks (D % 4 == 0, 16-byte aligned tensors): the
+  // double-buffered kernel; otherwise the synchronous one
+  const bool db = (D % 4) == 0 && (reinterpret_cast<uintptr_t>(q) & 15) == 0 &&
+                  (reinterpret_cast<uintptr_t>(k) & 15) == 0 && (reinterpret_cast<uintptr_t>(v) & 15) == 0 &&
+                  (reinterpret_cast<uintptr_t>(o) & 15) == 0;
+  auto kern = db ? attention_db_kernel<DP, kFast> : attention_kernel<DP, kFast>;
+  const int smem = db ? attention_db_smem_bytes<DP>() : attention_smem_bytes<DP>();
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
   if (e != cudaSuccess) return e;
   cudaLaunchConfig_t cfg = {};
