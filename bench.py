@@ -28,7 +28,6 @@ import re
 import statistics
 import subprocess
 import sys
-import threading
 import time
 
 import numpy as np
@@ -87,11 +86,38 @@ def profile_traffic(kernel, shard_cols):
     return None
 
 
+_SAMPLER_SRC = r"""
+import sys, time, pynvml
+uuids, period, out = sys.argv[1].split(","), float(sys.argv[2]), sys.argv[3]
+pynvml.nvmlInit()
+hs = []
+for i, u in enumerate(uuids):
+    try:
+        h = pynvml.nvmlDeviceGetHandleByUUID(u)
+    except Exception:
+        h = pynvml.nvmlDeviceGetHandleByIndex(i)
+    hs.append((i, h, pynvml.nvmlDeviceGetMaxClockInfo(h, pynvml.NVML_CLOCK_SM)))
+rs = getattr(pynvml, "nvmlDeviceGetCurrentClocksEventReasons", None) or pynvml.nvmlDeviceGetCurrentClocksThrottleReasons
+with open(out, "w", buffering=1) as f:
+    while True:
+        now = time.monotonic()
+        for i, h, mx in hs:
+            try:
+                f.write("%.6f %d %d %d %.3f %d\n" % (now, i, pynvml.nvmlDeviceGetClockInfo(h, pynvml.NVML_CLOCK_SM), mx,
+                                                     pynvml.nvmlDeviceGetPowerUsage(h) / 1000.0, int(rs(h))))
+            except Exception:
+                pass
+        time.sleep(period)
+"""
+
+
 class ClockSampler:
     """SM clock, power and clock-event (throttle) reasons of the given CUDA
-    devices, polled through NVML every few milliseconds from a background
-    thread, each sample time-stamped so that the samples inside the timed
-    region can be told from those of the warm-up around it."""
+    devices, polled through NVML every few milliseconds by a separate
+    process (so the sampling never competes with the launching thread for
+    the interpreter lock), each sample time-stamped on the system-wide
+    monotonic clock so that the samples inside the timed region can be told
+    from those of the warm-up around it."""
 
     REASONS = {0x4: "sw_power_cap", 0x8: "hw_slowdown", 0x20: "sw_thermal_slowdown", 0x40: "hw_thermal_slowdown",
                0x80: "hw_power_brake_slowdown"}
@@ -101,55 +127,52 @@ class ClockSampler:
         self.period = period_s
         self.rows = []  # (t, dev, sm_mhz, max_mhz, power_w, reason_bits)
         self.marks = {}
-        self._stop = threading.Event()
-        self.t = None
+        self.proc = None
+        self.path = None
         self.error = None
 
     def __enter__(self):
         try:
-            import pynvml
+            import tempfile
+
             import torch
 
-            pynvml.nvmlInit()
-            self.nv = pynvml
-            self.handles = []
+            uuids = []
             for d in self.devs:
-                try:
-                    uuid = str(torch.cuda.get_device_properties(d).uuid)
-                    h = pynvml.nvmlDeviceGetHandleByUUID(uuid if uuid.startswith("GPU-") else "GPU-" + uuid)
-                except Exception:  # noqa: BLE001
-                    h = pynvml.nvmlDeviceGetHandleByIndex(d)
-                self.handles.append((d, h, pynvml.nvmlDeviceGetMaxClockInfo(h, pynvml.NVML_CLOCK_SM)))
-            get_reasons = getattr(pynvml, "nvmlDeviceGetCurrentClocksEventReasons", None) or \
-                pynvml.nvmlDeviceGetCurrentClocksThrottleReasons
-            self._reasons = get_reasons
-            self.t = threading.Thread(target=self._run, daemon=True)
-            self.t.start()
+                u = str(torch.cuda.get_device_properties(d).uuid)
+                uuids.append(u if u.startswith("GPU-") else "GPU-" + u)
+            fd, self.path = tempfile.mkstemp(prefix="clocks_", suffix=".txt")
+            os.close(fd)
+            self.proc = subprocess.Popen([sys.executable, "-c", _SAMPLER_SRC, ",".join(uuids), str(self.period),
+                                          self.path], stdout=subprocess.DEVNULL, stderr=subprocess.DEVNULL)
+            time.sleep(0.2)  # NVML initialised and sampling before the window opens
         except Exception as e:  # noqa: BLE001
             self.error = f"{type(e).__name__}: {e}"[:200]
         return self
 
-    def _run(self):
-        nv = self.nv
-        while not self._stop.is_set():
-            now = time.perf_counter()
-            for d, h, mx in self.handles:
-                try:
-                    sm = nv.nvmlDeviceGetClockInfo(h, nv.NVML_CLOCK_SM)
-                    pw = nv.nvmlDeviceGetPowerUsage(h) / 1000.0
-                    rs = int(self._reasons(h))
-                    self.rows.append((now, d, sm, mx, pw, rs))
-                except Exception:  # noqa: BLE001
-                    pass
-            self._stop.wait(self.period)
-
     def mark(self, name):
-        self.marks[name] = time.perf_counter()
+        self.marks[name] = time.monotonic()
 
     def __exit__(self, *a):
-        self._stop.set()
-        if self.t:
-            self.t.join(timeout=2)
+        if self.proc:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except Exception:  # noqa: BLE001
+                self.proc.kill()
+            self.proc = None
+        if self.path and os.path.exists(self.path):
+            with open(self.path) as f:
+                for line in f:
+                    p = line.split()
+                    if len(p) == 6:
+                        try:
+                            self.rows.append((float(p[0]), self.devs[int(p[1])], int(p[2]), int(p[3]), float(p[4]),
+                                              int(p[5])))
+                        except (ValueError, IndexError):
+                            pass
+            os.unlink(self.path)
+            self.path = None
 
     def summary(self, begin="timed_begin", end="timed_end"):
         """Samples inside [begin, end]; when the region is shorter than the
@@ -170,7 +193,7 @@ class ClockSampler:
         return {"sm_mhz": statistics.median(r[2] for r in rows), "sm_max_mhz": max(r[3] for r in rows),
                 "sm_mhz_min": min(r[2] for r in rows), "reasons": reasons, "samples": len(rows),
                 "power_w_max": max(r[4] for r in rows), "scope": scope, "source": "NVML, polled every "
-                f"{self.period * 1e3:.0f} ms"}
+                f"{self.period * 1e3:.0f} ms by a separate process"}
 
 
 def cpu_port_run(x, wg, wu, rows, threads):
