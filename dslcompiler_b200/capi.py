@@ -120,6 +120,7 @@ PROTOTYPES = {
     "llk_status_string": (ctypes.c_char_p, [_i]),
     "llk_synchronize": (_i, [_i, _vp]),
     "llk_diag_timeout_probe": (_i, [_i, _i64]),
+    "llk_diag_reciprocal_check": (_i, [_i, ctypes.c_uint32, ctypes.c_uint32, _P(_u64)]),
     "llk_swiglu_decode_noalloc": (_i, [_P(Tensor2D), _P(Tensor2D), _P(Tensor2D), _P(Tensor2D), _vp,
                                       _P(GpuContext)]),
     "llk_pack_weights": (_i, [_P(Tensor2D), _P(Tensor2D), _P(GpuContext), _P(_vp)]),

@@ -1036,6 +1036,29 @@ int llk_synchronize(int device, void *stream) {
   return read_and_clear_status(*ds, static_cast<cudaStream_t>(stream));
 }
 
+int llk_diag_reciprocal_check(int device, uint32_t lo_bits, uint32_t hi_bits, uint64_t *mismatches) {
+  if (!mismatches || hi_bits < lo_bits) return LLK_ERR_ARG;
+  DeviceRestore restore;
+  llk_gpu_context g;
+  std::memset(&g, 0, sizeof(g));
+  g.device = device;
+  int dev, rc;
+  if ((rc = resolve_device(&g, &dev)) != LLK_OK) return rc;
+  DeviceState *ds;
+  if ((rc = device_init(dev, &ds)) != LLK_OK) return rc;
+  unsigned long long *d = nullptr;
+  if (cudaMalloc(&d, sizeof(*d)) != cudaSuccess) return LLK_ERR_NOMEM;
+  unsigned long long h = 0;
+  rc = LLK_OK;
+  if (cudaMemset(d, 0, sizeof(*d)) != cudaSuccess ||
+      diag_reciprocal_launch(d, lo_bits, hi_bits, ds->sm_count, nullptr) != cudaSuccess ||
+      cudaMemcpy(&h, d, sizeof(h), cudaMemcpyDeviceToHost) != cudaSuccess)
+    rc = LLK_ERR_CUDA;
+  cudaFree(d);
+  *mismatches = h;
+  return rc;
+}
+
 int llk_diag_timeout_probe(int device, int64_t limit_ns) {
   if (limit_ns <= 0) return LLK_ERR_ARG;
   DeviceRestore restore;

@@ -85,6 +85,15 @@ __device__ __forceinline__ bool mbar_wait_bounded(uint64_t *bar, uint32_t parity
   }
 }
 
+// 16-byte global -> shared copy through L2 (cp.async, no TMA), and the wait
+// for all of the thread's copies.
+__device__ __forceinline__ void cp_async_16(void *smem_dst, const void *gsrc) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(smem_dst)), "l"(gsrc) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit_wait_all() {
+  asm volatile("cp.async.commit_group;\n\tcp.async.wait_group 0;" ::: "memory");
+}
+
 // ------------------------------------------------------------------- TMA
 __device__ __forceinline__ void tma_prefetch_desc(const CUtensorMap *map) {
   asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
@@ -237,14 +246,84 @@ __device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
 // B200: 24 us against 22 us per tile at K = 4096; 5 us with __fdividef).
 __device__ __forceinline__ float silu_mul(float g, float u) { return __fdividef(g, 1.0f + __expf(-g)) * u; }
 
+// Correctly rounded reciprocal of b in [1, 2^126) by Markstein's method
+// (P. Markstein, "IA-64 and Elementary Functions", 2000, ch. 8): the
+// hardware's approximate reciprocal, then two residual corrections
+// e = 1 - b*y, y = y + e*y, each one FMA.  The result equals the IEEE
+// division 1.0f / b for every such b: checked against __frcp_rn over all
+// 2^30 floats of the range on a B200 (llk_diag_reciprocal_check).  No check
+// of the range here; rcp_rn_ge1 adds it.
+__device__ __forceinline__ float rcp_rn_markstein(float b) {
+  float y;
+  asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(b));
+  float e = fmaf(-b, y, 1.0f);
+  y = fmaf(e, y, y);
+  e = fmaf(-b, y, 1.0f);
+  return fmaf(e, y, y);
+}
+
+// 1 / b correctly rounded for b >= 1: Markstein's method in its range, CUDA's
+// correctly rounded reciprocal where the result would be denormal or zero.
+__device__ __forceinline__ float rcp_rn_ge1(float b) {
+  if (!(b < 0x1p126f)) return __frcp_rn(b);
+  return rcp_rn_markstein(b);
+}
+
 // The strict epilogue of the fused lowering (the reference's math.exp /
 // arith.divf sequence, lib/Transforms/FuseDoubleContraction.cpp:189-196):
-// sigmoid = 1 / (1 + exp(-g)) with CUDA's accurate expf and the IEEE-rounded
-// division, silu = g * sigmoid, r = silu * u -- the same operations in the
-// same order.
+// sigmoid = 1 / (1 + exp(-g)) with CUDA's accurate expf and the reciprocal
+// correctly rounded (the same value as the IEEE division), silu = g *
+// sigmoid, r = silu * u -- the same operations in the same order.
 __device__ __forceinline__ float silu_mul_strict(float g, float u) {
-  const float sigmoid = 1.0f / (1.0f + expf(-g));
+  const float sigmoid = rcp_rn_ge1(1.0f + expf(-g));
   return (g * sigmoid) * u;
+}
+
+// y[j] = SiLU(g[j]) * u[j] for a block of N elements (bit patterns of f32,
+// as tcgen05.ld returns them), strict or fast.  The strict block checks the
+// reciprocal's range outside its unrolled loop and redoes the rare elements
+// with 1 + e^-g >= 2^126 (g < -87) afterwards, so the common path stays
+// straight-line code: a full '/' made each tile's epilogue slower than its
+// MMAs, and a branch per element still cost half the epilogue's throughput
+// (measured on B200: 12 -> 5.6 us per 256 x 128 tile).
+template <bool kFast, int N>
+__device__ __forceinline__ void silu_mul_block(const uint32_t (&gb)[N], const uint32_t (&ub)[N], float (&y)[N]) {
+  float g[N], u[N];
+#pragma unroll
+  for (int j = 0; j < N; ++j) {
+    g[j] = __uint_as_float(gb[j]);
+    u[j] = __uint_as_float(ub[j]);
+  }
+  if constexpr (kFast) {
+#pragma unroll
+    for (int j = 0; j < N; ++j) y[j] = silu_mul(g[j], u[j]);
+  } else {
+    float x[N];
+    bool rare = false;
+#pragma unroll
+    for (int j = 0; j < N; ++j) {
+      x[j] = 1.0f + expf(-g[j]);
+      rare |= !(x[j] < 0x1p126f);
+    }
+#pragma unroll
+    for (int j = 0; j < N; ++j) y[j] = (g[j] * rcp_rn_markstein(x[j])) * u[j];
+    if (rare) {
+#pragma unroll
+      for (int j = 0; j < N; ++j)
+        if (!(x[j] < 0x1p126f)) y[j] = (g[j] * __frcp_rn(x[j])) * u[j];
+    }
+  }
+}
+
+template <bool kFast, int N>
+__device__ __forceinline__ void silu_mul_block(const float (&g)[N], const float (&u)[N], float (&y)[N]) {
+  uint32_t gb[N], ub[N];
+#pragma unroll
+  for (int j = 0; j < N; ++j) {
+    gb[j] = __float_as_uint(g[j]);
+    ub[j] = __float_as_uint(u[j]);
+  }
+  silu_mul_block<kFast, N>(gb, ub, y);
 }
 
 // Epilogue by math mode: kFast = bounded/unsafe fast (silu_mul), else strict.

@@ -129,4 +129,24 @@ cudaError_t diag_timeout_launch(int *status, uint64_t limit_ns, cudaStream_t str
   diag_timeout_kernel<<<1, 32, 0, stream>>>(status, limit_ns);
   return cudaGetLastError();
 }
+
+// The strict epilogue's reciprocal (rcp_rn_ge1) against CUDA's correctly
+// rounded reciprocal on every float whose bit pattern is in [lo, hi).
+namespace {
+__global__ void diag_reciprocal_kernel(unsigned long long *mismatches, uint32_t lo, uint32_t hi) {
+  unsigned long long n = 0;
+  for (uint64_t i = lo + static_cast<uint64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < hi;
+       i += static_cast<uint64_t>(gridDim.x) * blockDim.x) {
+    const float b = __uint_as_float(static_cast<uint32_t>(i));
+    if (__float_as_uint(rcp_rn_ge1(b)) != __float_as_uint(__frcp_rn(b))) ++n;
+  }
+  if (n) atomicAdd(mismatches, n);
+}
+}  // namespace
+
+cudaError_t diag_reciprocal_launch(unsigned long long *mismatches, uint32_t lo, uint32_t hi, int sm_count,
+                                   cudaStream_t stream) {
+  diag_reciprocal_kernel<<<8 * sm_count, 256, 0, stream>>>(mismatches, lo, hi);
+  return cudaGetLastError();
+}
 }  // namespace llk_b200

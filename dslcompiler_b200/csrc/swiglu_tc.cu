@@ -223,8 +223,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           const int col = n0 + c;
           if (row < p.M && col < p.N) {
             float y[32];
-#pragma unroll
-            for (int j = 0; j < 32; ++j) y[j] = silu_mul_mode<kFast>(__uint_as_float(g[j]), __uint_as_float(u[j]));
+            silu_mul_block<kFast, 32>(g, u, y);
             if (kMode == TC_SWIGLU_BF16) {
               uint16_t *dst = reinterpret_cast<uint16_t *>(p.y) + (int64_t)row * p.ldy + col;
               if (p.vec_ok && col + 32 <= p.N) {

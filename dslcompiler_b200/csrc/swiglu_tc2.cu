@@ -117,7 +117,8 @@ __device__ __forceinline__ bool item_to_work(const TcParams &p, int n_pairs, int
 // 512 contiguous bytes.  Returns false when the wait gave up.
 template <int MODE>
 __device__ __forceinline__ bool ksplit_epilogue(const TcParams &p, const Work &w, int tl, uint32_t rank, int q,
-                                                int lane, uint32_t t_row, int m0, int n0, volatile int *abort) {
+                                                int lane, uint32_t t_row, int m0, int n0, volatile int *abort,
+                                                float4 *stash) {
   constexpr int kMode = MODE & ~TC_FAST_MATH;
   constexpr bool kFast = (MODE & TC_FAST_MATH) != 0;
   constexpr bool kSwiglu = (kMode == TC_SWIGLU_BF16 || kMode == TC_SWIGLU_F32);
@@ -174,7 +175,33 @@ __device__ __forceinline__ bool ksplit_epilogue(const TcParams &p, const Work &w
   ok = __shfl_sync(0xffffffffu, ok, 0);
   if (!ok) return false;
   __threadfence();
+  // Gather the other parts' sums of this thread's row for every owned chunk
+  // into shared memory at once (cp.async: one round trip through L2 for all
+  // of them instead of one per part), then add in part order.  The stash is
+  // the pipeline ring, idle once this pair's last item -- the tail part --
+  // has its accumulator complete: entry k of thread r at float4 k * 128 + r
+  // (consecutive lanes, consecutive 16 bytes).  At most 96 entries per
+  // thread (7 other parts x 2 owned chunks x 8 float4): 192 KB, the ring.
+  constexpr int kPer = kSwiglu ? 8 : 4;  // float4s of one row per (chunk, part)
+  int k = 0;
+#pragma unroll 1
+  for (int c = w.part; c < kChunks; c += s) {
+    for (int part = 0; part < s; ++part) {
+      if (part == w.part) continue;
+      const float4 *pb = tail + ((tile_base + part * 2 + rank) * kBlock) + r;
+#pragma unroll
+      for (int i = 0; i < 4; ++i) cp_async_16(stash + (size_t)(k + i) * 128 + r, pb + (size_t)(4 * c + i) * 128);
+      if (kSwiglu) {
+#pragma unroll
+        for (int i = 0; i < 4; ++i)
+          cp_async_16(stash + (size_t)(k + 4 + i) * 128 + r, pb + (size_t)(32 + 4 * c + i) * 128);
+      }
+      k += kPer;
+    }
+  }
+  cp_async_commit_wait_all();
   const int row = m0 + r;
+  k = 0;
 #pragma unroll 1
   for (int c = w.part; c < kChunks; c += s) {
     uint32_t a[16], b[16];
@@ -191,24 +218,24 @@ __device__ __forceinline__ bool ksplit_epilogue(const TcParams &p, const Work &w
           ga[j] += __uint_as_float(a[j]);
           if (kSwiglu) ua[j] += __uint_as_float(b[j]);
         }
-      } else {
-        const float4 *pb = tail + ((tile_base + part * 2 + rank) * kBlock) + r;
+        continue;
+      }
 #pragma unroll
-        for (int i = 0; i < 4; ++i) {
-          const float4 v = __ldcg(pb + (size_t)(4 * c + i) * 128);
-          ga[4 * i] += v.x;
-          ga[4 * i + 1] += v.y;
-          ga[4 * i + 2] += v.z;
-          ga[4 * i + 3] += v.w;
-          if (kSwiglu) {
-            const float4 u = __ldcg(pb + (size_t)(32 + 4 * c + i) * 128);
-            ua[4 * i] += u.x;
-            ua[4 * i + 1] += u.y;
-            ua[4 * i + 2] += u.z;
-            ua[4 * i + 3] += u.w;
-          }
+      for (int i = 0; i < 4; ++i) {
+        const float4 v = stash[(size_t)(k + i) * 128 + r];
+        ga[4 * i] += v.x;
+        ga[4 * i + 1] += v.y;
+        ga[4 * i + 2] += v.z;
+        ga[4 * i + 3] += v.w;
+        if (kSwiglu) {
+          const float4 u = stash[(size_t)(k + 4 + i) * 128 + r];
+          ua[4 * i] += u.x;
+          ua[4 * i + 1] += u.y;
+          ua[4 * i + 2] += u.z;
+          ua[4 * i + 3] += u.w;
         }
       }
+      k += kPer;
     }
     const int col = n0 + 16 * c;
     if (row >= p.M || col >= p.N) continue;
@@ -216,8 +243,7 @@ __device__ __forceinline__ bool ksplit_epilogue(const TcParams &p, const Work &w
     const bool vec = p.vec_ok && col + 16 <= p.N;
     if (kSwiglu) {
       float y[16];
-#pragma unroll
-      for (int j = 0; j < 16; ++j) y[j] = silu_mul_mode<kFast>(ga[j], ua[j]);
+      silu_mul_block<kFast, 16>(ga, ua, y);
       for (int t = -1; t < p.n_peers; ++t) {
         void *base = t < 0 ? p.y : p.y_peers[t];
         if (kMode == TC_SWIGLU_BF16) {
@@ -564,7 +590,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       const int row = m0 + row_in_tile;
       const uint32_t t_row = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + acc * kMmaN;
       if (w.nparts > 1) {
-        if (!ksplit_epilogue<MODE>(p, w, w.tile - p.dp_waves * n_pairs, rank, q, lane, t_row, m0, n0, abort)) {
+        if (!ksplit_epilogue<MODE>(p, w, w.tile - p.dp_waves * n_pairs, rank, q, lane, t_row, m0, n0, abort,
+                                   reinterpret_cast<float4 *>(smem))) {
           ok = false;
           break;
         }
@@ -587,8 +614,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           const int col = n0 + c;
           if (r0 >= p.M || col >= p.N) continue;  // warp-uniform
           float y[32];
-#pragma unroll
-          for (int j = 0; j < 32; ++j) y[j] = silu_mul_mode<kFast>(__uint_as_float(g[j]), __uint_as_float(u[j]));
+          silu_mul_block<kFast, 32>(g, u, y);
           const uint32_t buf = wstage + static_cast<uint32_t>(y_chunks % kNBuf) * kBuf;
           // lanes that store (one per map) wait until their store of this
           // buffer's previous chunk has read it
@@ -631,8 +657,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           const int col = n0 + c;
           if (row < p.M && col < p.N) {
             float y[32];
-#pragma unroll
-            for (int j = 0; j < 32; ++j) y[j] = silu_mul_mode<kFast>(__uint_as_float(g[j]), __uint_as_float(u[j]));
+            silu_mul_block<kFast, 32>(g, u, y);
             const int64_t off = (int64_t)row * p.ldy + col;
             const bool vec = p.vec_ok && col + 32 <= p.N;
             if (kMode == TC_SWIGLU_BF16) {

@@ -112,5 +112,9 @@ cudaError_t simt_launch(int mode, const void *x, int64_t ldx, int64_t sxk, const
 
 // Diagnostic: a bounded wait that is made to expire (see swiglu_simt.cu).
 cudaError_t diag_timeout_launch(int *status, uint64_t limit_ns, cudaStream_t stream);
+// Diagnostic: counts the floats with bit patterns in [lo, hi) on which the
+// strict epilogue's reciprocal differs from CUDA's correctly rounded one.
+cudaError_t diag_reciprocal_launch(unsigned long long *mismatches, uint32_t lo, uint32_t hi, int sm_count,
+                                   cudaStream_t stream);
 
 }  // namespace llk_b200

@@ -192,6 +192,14 @@ int llk_synchronize(int device, void *stream);
  * GPU without a fault or a hang. */
 int llk_diag_timeout_probe(int device, int64_t limit_ns);
 
+/* Diagnostic: the strict SwiGLU epilogue computes 1 / (1 + e^-g) with its
+ * own correctly rounded reciprocal (Markstein's method) instead of the
+ * general IEEE division; this counts, into *mismatches, the floats with bit
+ * patterns in [lo_bits, hi_bits) on which it differs from CUDA's correctly
+ * rounded reciprocal.  0 over [0x3f800000, 0x7f800000) (every finite b >= 1)
+ * shows the epilogue equals the division.  No counterpart in the reference. */
+int llk_diag_reciprocal_check(int device, uint32_t lo_bits, uint32_t hi_bits, uint64_t *mismatches);
+
 /* ---- decode without device allocation -------------------------------- */
 
 /* Size of the fixed device scratch array behind llk_swiglu_decode_noalloc

@@ -127,3 +127,14 @@ def test_math_modes_select_different_kernels_and_match_oracle(M, K, N, variant):
             key = llk.KernelKey(N=N, K=K, M_bucket=llk.classify_m(M), output_type=capi.LLK_DTYPE_FP32,
                                 thread_count=capi.VARIANTS[variant], math_mode=capi.MATH_MODES[mode])
             assert key.find() is not None, mode
+
+
+def test_strict_epilogue_reciprocal_equals_ieee_division():
+    """The strict epilogue's own reciprocal (Markstein's method) gives the
+    correctly rounded 1/b, i.e. the IEEE division 1.0f / b, for every finite
+    float b >= 1 (the range of 1 + e^-g): all 2^30 of them, on the GPU."""
+    import ctypes
+
+    n = ctypes.c_uint64(123)
+    assert capi.lib().llk_diag_reciprocal_check(0, 0x3F800000, 0x7F800000, ctypes.byref(n)) == capi.LLK_OK
+    assert n.value == 0
