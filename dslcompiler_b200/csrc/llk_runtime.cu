@@ -145,6 +145,22 @@ int device_init(int dev, DeviceState **out) {
   return LLK_OK;
 }
 
+// Where a buffer lives, from one pointer query: 0 = host (or unknown to
+// CUDA), 1 = device memory of `dev` or managed memory, -1 = device memory
+// of another GPU (the kernels on `dev` would fault on it unless peer access
+// happens to be enabled, so the entry points that launch on `dev` refuse it).
+int locate_ptr(const void *p, int dev) {
+  if (!p) return 0;
+  cudaPointerAttributes a;
+  if (cudaPointerGetAttributes(&a, p) != cudaSuccess) {
+    cudaGetLastError();
+    return 0;
+  }
+  if (a.type == cudaMemoryTypeManaged) return 1;
+  if (a.type != cudaMemoryTypeDevice) return 0;
+  return a.device == dev ? 1 : -1;
+}
+
 bool is_device_ptr(const void *p) {
   if (!p) return false;
   cudaPointerAttributes a;
@@ -733,11 +749,11 @@ int run_op(int op, const Tensor2D *x, const Tensor2D *wg, const Tensor2D *wu, Te
   bool any_host;
   {
     // Where each buffer lives, asked once per call.
-    const bool dx = is_device_ptr(x->data), dy = is_device_ptr(y->data);
-    const bool dg = packed_g ? true : is_device_ptr(wg->data);
-    const bool du = packed_g ? true : (wu == wg ? dg : is_device_ptr(wu->data));
-    if ((dx && on_other_device(x->data, dev)) || (dy && on_other_device(y->data, dev)) ||
-        (!packed_g && dg && on_other_device(wg->data, dev)) || (!packed_g && du && on_other_device(wu->data, dev)))
+    const int lx = locate_ptr(x->data, dev), ly = locate_ptr(y->data, dev);
+    const int lg = packed_g ? 1 : locate_ptr(wg->data, dev);
+    const int lu = packed_g ? 1 : (wu == wg ? lg : locate_ptr(wu->data, dev));
+    const bool dx = lx != 0, dy = ly != 0, dg = lg != 0, du = lu != 0;
+    if (lx < 0 || ly < 0 || lg < 0 || lu < 0)
       return LLK_ERR_ARG;
     std::lock_guard<std::mutex> lk(ds->mu);
     if (op == LLK_OP_FUSED_SWIGLU && !packed_g && x->data && wg->data && wu->data && y->data && !dx && !dg && !du &&

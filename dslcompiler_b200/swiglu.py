@@ -37,7 +37,7 @@ def tensor2d(t) -> Tensor2D:
     if _is_torch(t):
         if t.dim() != 2:
             raise ValueError("expected a 2-D tensor")
-        return Tensor2D(t.data_ptr(), t.shape[0], t.shape[1], t.stride(0), t.stride(1))
+        return Tensor2D(t.data_ptr(), *t.shape, *t.stride())
     a = t
     if not isinstance(a, np.ndarray) or a.ndim != 2:
         raise ValueError("expected a 2-D torch tensor or numpy array")
@@ -49,8 +49,17 @@ def _stream_of(t, stream):
     if stream is not None:
         return stream.cuda_stream if hasattr(stream, "cuda_stream") else int(stream)
     if _is_torch(t) and t.is_cuda:
-        return torch.cuda.current_stream(t.device).cuda_stream
+        return _current_raw_stream(t.device.index)
     return None
+
+
+def _current_raw_stream(index):
+    """cudaStream_t of torch's current stream on device `index` (None = the
+    current device), without building a torch.cuda.Stream object."""
+    if index is None:
+        index = torch.cuda.current_device()
+    raw = getattr(torch._C, "_cuda_getCurrentRawStream", None)
+    return raw(index) if raw is not None else torch.cuda.current_stream(index).cuda_stream
 
 
 def _device_of(t, device):
@@ -104,13 +113,14 @@ def fused_swiglu(x, wg, wu, *, out=None, out_dtype: str = "bf16", variant: str =
     if out is None:
         out = _new_out(x, x.shape[0], wg.shape[1], f32)
     tx, tg, tu, ty = tensor2d(x), tensor2d(wg), tensor2d(wu), tensor2d(out)
-    ctx = KernelContext(None, 0)
+    ctx = None  # no scratch: the library's own workspace
     if scratch is not None:
         ctx = KernelContext(scratch.data_ptr(), scratch.numel() * scratch.element_size())
     g = gpu_context(_device_of(x, device), _stream_of(x, stream),
                     capi.LLK_DTYPE_FP32 if f32 else capi.LLK_DTYPE_BF16, variant, math_mode)
-    check(lib().llk_swiglu_ex(ctypes.byref(tx), ctypes.byref(tg), ctypes.byref(tu), ctypes.byref(ty),
-                              ctypes.byref(ctx), ctypes.byref(g)), "llk_swiglu_ex")
+    rc = lib().llk_swiglu_ex(tx, tg, tu, ty, ctx, g)
+    if rc:
+        check(rc, "llk_swiglu_ex")
     return out
 
 
