@@ -809,7 +809,12 @@ struct BarrierArgs {
 // Thread r < n: publish `epoch` in rank r's slot for this rank (system-scope
 // release), then wait until rank r published it here.  Bounded: after the
 // limit the status word gets LLK_ERR_TIMEOUT and the kernel returns.
+// Launched as a programmatic dependent of the SwiGLU kernel before it: the
+// launch overlaps that kernel's tail, and griddepcontrol.wait returns once
+// it has completed and its memory operations (the peer stores) are
+// performed, so nothing is published early.
 __global__ void peer_barrier_kernel(BarrierArgs a, int n, unsigned int epoch, int *status) {
+  asm volatile("griddepcontrol.wait;" ::: "memory");
   const int r = threadIdx.x;
   if (r >= n) return;
   __threadfence_system();
@@ -1687,8 +1692,18 @@ int llk_swiglu_column_parallel(const Tensor2D *x, const Tensor2D *wg_shard, cons
           return LLK_ERR_CUDA;
     }
   }
-  peer_barrier_kernel<<<1, 32, 0, stream>>>(exit_, g->n, g->epoch, ds->status);
-  return cudaGetLastError() == cudaSuccess ? LLK_OK : LLK_ERR_CUDA;
+  cudaLaunchConfig_t cfg = {};
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.gridDim = dim3(1);
+  cfg.blockDim = dim3(32);
+  cfg.stream = stream;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, peer_barrier_kernel, exit_, g->n, g->epoch, ds->status) == cudaSuccess
+             ? LLK_OK
+             : LLK_ERR_CUDA;
 }
 
 }  // extern "C"
