@@ -60,13 +60,19 @@ def measured_peaks():
 
 
 def choose_peak(peaks, region_s, clocks):
-    """The bf16 denominator for a timed region: the sustained figure only when
-    the region ran long enough to reach the power cap (over one second) AND
-    its own clock samples show sw_power_cap; the burst figure otherwise."""
+    """The bf16 denominator for a timed region: the sustained figure when its
+    own clock samples show sw_power_cap AND the cap held the clock down (the
+    region ran over one second, or its median SM clock was under 0.9 of the
+    maximum); the burst figure otherwise."""
     capped = bool(clocks) and "sw_power_cap" in (clocks.get("reasons") or [])
-    if region_s > 1.0 and capped:
-        return peaks["sustained"], "sustained", f"region {region_s:.3f} s with sw_power_cap in its clock samples"
-    why = "no sw_power_cap in its clock samples" if not capped else "shorter than 1 s"
+    held = False
+    if capped:
+        med, top = clocks.get("sm_mhz"), clocks.get("sm_max_mhz")
+        held = region_s > 1.0 or (med is not None and top and med < 0.9 * top)
+    if held:
+        return peaks["sustained"], "sustained", (f"region {region_s:.3f} s with sw_power_cap in its clock samples, "
+                                                 f"median SM clock {clocks.get('sm_mhz')} of {clocks.get('sm_max_mhz')} MHz")
+    why = "no sw_power_cap in its clock samples" if not capped else "the power cap did not hold the clock down"
     return peaks["burst"], "burst", f"region {region_s:.3f} s, {why}"
 
 
