@@ -1036,6 +1036,25 @@ def profile_case(args):
     import dslcompiler_b200 as llk
     from dslcompiler_b200 import datagen as dg
 
+    if args.profile_case == "attention":
+        # --shape B,H,L,D: causal self-attention, f32 (the Llama-7B attention
+        # shape is 1,32,2048,128)
+        B_, H_, L_, D_ = (int(v) for v in (args.shape or "1,32,2048,128").split(","))
+        g = torch.Generator(device="cuda").manual_seed(42)
+        q, k, v = (torch.randn((B_, H_, L_, D_), generator=g, device="cuda") for _ in range(3))
+        o = torch.zeros_like(q)
+        s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        times = []
+        for _ in range(args.launches):
+            s.record()
+            llk.attention(q, k, v, scale=D_ ** -0.5, causal=True, out=o)
+            e.record()
+            torch.cuda.synchronize()
+            times.append(s.elapsed_time(e))
+        llk.synchronize(0)
+        print(f"attention B={B_} H={H_} L={L_} D={D_}: {args.launches} launches, ms per launch "
+              f"{[round(t, 4) for t in times]}", file=sys.stderr)
+        return 0
     if args.profile_case == "shape":
         M_, K_, N_ = (int(v) for v in args.shape.split(","))
         c = dict(kind="swiglu", M=M_, K=K_, N=N_, x_std=1.0, w_std=0.02, y="bf16")
@@ -1078,7 +1097,8 @@ def main(argv=None):
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--profile-case", default=None, metavar="CFG",
                     help="run one configuration's kernel --launches times on cuda:0 (for ncu) and exit; CFG is a "
-                         "config name (c1 .. c5, c4_m1 ..) or 'shape' with --shape M,K,N")
+                         "config name (c1 .. c5, c4_m1 ..), 'shape' with --shape M,K,N, or 'attention' with "
+                         "--shape B,H,L,D (causal f32 attention)")
     ap.add_argument("--shape", default=None)
     ap.add_argument("--launches", type=int, default=3)
     ap.add_argument("--variant", default="auto")
