@@ -142,6 +142,18 @@ __device__ __forceinline__ float exp_mode(float v) {
   }
 }
 
+// Query tile and head of this CTA.  The grid is one-dimensional over
+// (query tile, head) with the LAST query tiles first: under a causal mask a
+// tile's work grows with its index, so the heaviest CTAs start in the first
+// wave and the light ones fill the end (longest-first order).
+__device__ __forceinline__ void tile_of_block(int64_t Lq, int64_t &bh, int64_t &q0) {
+  const int64_t n_qt = (Lq + kBQ - 1) / kBQ;
+  const int64_t BH = static_cast<int64_t>(gridDim.x) / n_qt;
+  const int64_t i = blockIdx.x;
+  bh = i % BH;
+  q0 = (n_qt - 1 - i / BH) * kBQ;
+}
+
 // Thread layout: ty = tid / 16 owns query rows 4*ty .. 4*ty+3 of the tile;
 // tx = tid % 16 owns key columns 4*tx .. 4*tx+3 of the score tile and output
 // columns {4*tx + 64*j .. +3} (j < DP/64).  The 16 threads of a row group are
@@ -161,8 +173,8 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
 
   const int tid = threadIdx.x;
   const int ty = tid >> 4, tx = tid & 15;
-  const int64_t bh = blockIdx.y;
-  const int64_t q0 = static_cast<int64_t>(blockIdx.x) * kBQ;
+  int64_t bh, q0;
+  tile_of_block(Lq, bh, q0);
   const float *qb = q + bh * Lq * D;
   const float *kb = k + bh * Lk * D;
   const float *vb = v + bh * Lk * D;
@@ -364,8 +376,8 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
 
   const int tid = threadIdx.x;
   const int ty = tid >> 4, tx = tid & 15;
-  const int64_t bh = blockIdx.y;
-  const int64_t q0 = static_cast<int64_t>(blockIdx.x) * kBQ;
+  int64_t bh, q0;
+  tile_of_block(Lq, bh, q0);
   const float *qb = q + bh * Lq * D;
   const float *kb = k + bh * Lk * D;
   const float *vb = v + bh * Lk * D;
@@ -425,13 +437,21 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
     for (int i = 0; i < 4; ++i)
 #pragma unroll
       for (int j = 0; j < 4; ++j) s[i][j] = 0.f;
-#pragma unroll 2
+    // operands of step d + 4 are loaded while step d computes (registers
+    // double-buffered: the shared-memory latency overlaps the FMAs)
+    float4 a[4], b[4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) a[i] = *reinterpret_cast<const float4 *>(&Qs[(4 * ty + i) * kLd]);
+#pragma unroll
+    for (int j = 0; j < 4; ++j) b[j] = *reinterpret_cast<const float4 *>(&Ks[(tx + 16 * j) * kLd]);
+#pragma unroll 4
     for (int d = 0; d < DP; d += 4) {
-      float4 a[4], b[4];
+      float4 an[4], bn[4];
+      const int dn = d + 4 < DP ? d + 4 : d;
 #pragma unroll
-      for (int i = 0; i < 4; ++i) a[i] = *reinterpret_cast<const float4 *>(&Qs[(4 * ty + i) * kLd + d]);
+      for (int i = 0; i < 4; ++i) an[i] = *reinterpret_cast<const float4 *>(&Qs[(4 * ty + i) * kLd + dn]);
 #pragma unroll
-      for (int j = 0; j < 4; ++j) b[j] = *reinterpret_cast<const float4 *>(&Ks[(tx + 16 * j) * kLd + d]);
+      for (int j = 0; j < 4; ++j) bn[j] = *reinterpret_cast<const float4 *>(&Ks[(tx + 16 * j) * kLd + dn]);
 #pragma unroll
       for (int i = 0; i < 4; ++i)
 #pragma unroll
@@ -441,6 +461,11 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
           s[i][j] = fmaf(a[i].z, b[j].z, s[i][j]);
           s[i][j] = fmaf(a[i].w, b[j].w, s[i][j]);
         }
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        a[i] = an[i];
+        b[i] = bn[i];
+      }
     }
     float p[4][4];
 #pragma unroll
@@ -479,13 +504,21 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
       *reinterpret_cast<float4 *>(&Pt[(tx + 16 * j) * (kBQ + kPad) + 4 * ty]) =
           make_float4(p[0][j], p[1][j], p[2][j], p[3][j]);
     __syncthreads();
-#pragma unroll 4
+    float4 pr = *reinterpret_cast<const float4 *>(&Pt[4 * ty]);
+    float4 vr[kOC];
+#pragma unroll
+    for (int jj = 0; jj < kOC; ++jj) vr[jj] = *reinterpret_cast<const float4 *>(&Vs[64 * jj + 4 * tx]);
+#pragma unroll 8
     for (int kk = 0; kk < kBK; ++kk) {
-      const float4 pr = *reinterpret_cast<const float4 *>(&Pt[kk * (kBQ + kPad) + 4 * ty]);
+      const int kn = kk + 1 < kBK ? kk + 1 : kk;
+      const float4 prn = *reinterpret_cast<const float4 *>(&Pt[kn * (kBQ + kPad) + 4 * ty]);
+      float4 vrn[kOC];
+#pragma unroll
+      for (int jj = 0; jj < kOC; ++jj) vrn[jj] = *reinterpret_cast<const float4 *>(&Vs[kn * kLd + 64 * jj + 4 * tx]);
       const float pv[4] = {pr.x, pr.y, pr.z, pr.w};
 #pragma unroll
       for (int jj = 0; jj < kOC; ++jj) {
-        const float4 vv = *reinterpret_cast<const float4 *>(&Vs[kk * kLd + 64 * jj + 4 * tx]);
+        const float4 vv = vr[jj];
 #pragma unroll
         for (int i = 0; i < 4; ++i) {
           acc[i][jj][0] = fmaf(pv[i], vv.x, acc[i][jj][0]);
@@ -494,6 +527,9 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
           acc[i][jj][3] = fmaf(pv[i], vv.w, acc[i][jj][3]);
         }
       }
+      pr = prn;
+#pragma unroll
+      for (int jj = 0; jj < kOC; ++jj) vr[jj] = vrn[jj];
     }
     __syncthreads();  // Pt and this stage's K / V are free for the next loads
   }
@@ -546,7 +582,7 @@ cudaError_t launch_attention_dp(const float *q, const float *k, const float *v, 
   cudaLaunchAttribute attr[1];
   attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
   attr[0].val.programmaticStreamSerializationAllowed = 1;
-  cfg.gridDim = dim3(static_cast<unsigned>((Lq + kBQ - 1) / kBQ), static_cast<unsigned>(BH));
+  cfg.gridDim = dim3(static_cast<unsigned>((Lq + kBQ - 1) / kBQ * BH));  // see tile_of_block
   cfg.blockDim = dim3(kAttnThreads);
   cfg.dynamicSmemBytes = smem;
   cfg.stream = stream;
@@ -616,8 +652,10 @@ cudaError_t rope_launch(const float *x, const int64_t *pos, float *y, int64_t B,
 }
 
 bool attention_supported(int64_t B, int64_t H, int64_t Lq, int64_t Lk, int64_t D) {
+  // grid: (Lq / 64) x B x H CTAs in one dimension (D <= 128), or (Lq / 8)
+  // x (B x H) in two
   return B >= 0 && H >= 0 && Lq >= 0 && Lk >= 0 && D >= 1 && D <= 4096 && B * H <= 65535 &&
-         (Lq + 63) / 64 <= INT32_MAX;
+         (Lq + 63) / 64 * B * H <= INT32_MAX && (Lq + 7) / 8 <= INT32_MAX;
 }
 
 cudaError_t attention_launch(const float *q, const float *k, const float *v, float *o, int64_t B, int64_t H,
