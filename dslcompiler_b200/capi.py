@@ -121,6 +121,8 @@ PROTOTYPES = {
     "llk_synchronize": (_i, [_i, _vp]),
     "llk_diag_timeout_probe": (_i, [_i, _i64]),
     "llk_diag_reciprocal_check": (_i, [_i, ctypes.c_uint32, ctypes.c_uint32, _P(_u64)]),
+    "llk_diag_pair_schedule": (_i, [_i, _i64, _i64, _i64, _i, _i, _i, _P(ctypes.c_int32), _i, _P(_i), _P(_i), _P(_i),
+                                    _P(_i)]),
     "llk_swiglu_decode_noalloc": (_i, [_P(Tensor2D), _P(Tensor2D), _P(Tensor2D), _P(Tensor2D), _vp,
                                       _P(GpuContext)]),
     "llk_pack_weights": (_i, [_P(Tensor2D), _P(Tensor2D), _P(GpuContext), _P(_vp)]),

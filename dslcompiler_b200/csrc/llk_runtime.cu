@@ -1080,6 +1080,17 @@ int llk_diag_reciprocal_check(int device, uint32_t lo_bits, uint32_t hi_bits, ui
   return rc;
 }
 
+int llk_diag_pair_schedule(int swiglu, int64_t M, int64_t N, int64_t K, int pairs, int tail_split, int dynamic,
+                           int32_t *items, int max_items, int *n_items, int *n_pairs, int *ksplit, int *tail_split_out) {
+  if (!n_items || !n_pairs || !ksplit || !tail_split_out || (max_items > 0 && !items) || max_items < 0)
+    return LLK_ERR_ARG;
+  // the library workspace of a 148-SM device (room for the K-split tail)
+  return tc2_schedule_items(swiglu, M, N, K, pairs, tail_split, dynamic, tc2_tail_workspace_bytes(2 * pairs), items,
+                            max_items, n_items, n_pairs, ksplit, tail_split_out) == 0
+             ? LLK_OK
+             : LLK_ERR_ARG;
+}
+
 int llk_diag_timeout_probe(int device, int64_t limit_ns) {
   if (limit_ns <= 0) return LLK_ERR_ARG;
   DeviceRestore restore;

@@ -37,6 +37,7 @@
 
 #include <atomic>
 #include <cstdint>
+#include <cstring>
 
 #include "sm100_ptx.cuh"
 #include "tc_kernels.h"
@@ -74,7 +75,7 @@ struct Work {
 // dp_waves x pairs), the rest are the parts of the leftover tiles: ksplit
 // K parts each, or else tail_split column parts.  False past the last item.
 template <int TILE_N>
-__device__ __forceinline__ bool item_to_work(const TcParams &p, int n_pairs, int item, Work &w) {
+__host__ __device__ __forceinline__ bool item_to_work(const TcParams &p, int n_pairs, int item, Work &w) {
   const int whole = p.dp_waves * n_pairs;
   w.c0 = 0;
   w.wn = TILE_N;
@@ -295,11 +296,11 @@ __device__ __forceinline__ bool ksplit_epilogue(const TcParams &p, const Work &w
 
 // Row block and column tile of a tile index: bands of p.group_m row blocks,
 // row block fastest inside a band (the last band may be narrower).
-__device__ __forceinline__ void tile_coords(const TcParams &p, int tile, int &mt, int &nt) {
+__host__ __device__ __forceinline__ void tile_coords(const TcParams &p, int tile, int &mt, int &nt) {
   const int per_band = p.group_m * p.n_tiles;
   const int band = tile / per_band;
   const int r = tile - band * per_band;
-  const int rows = min(p.group_m, p.m_tiles - band * p.group_m);
+  const int rows = p.group_m < p.m_tiles - band * p.group_m ? p.group_m : p.m_tiles - band * p.group_m;
   mt = band * p.group_m + r % rows;
   nt = r / rows;
 }
@@ -790,42 +791,21 @@ constexpr size_t kTailBlockBytes = 128 * 256 * sizeof(float);
 // leftover tile, CTA and epilogue warp).
 constexpr int kMaxTailTiles = static_cast<int>((kWsTc2CounterBytes - kWsTc2TailCounters) / (2 * 4 * 2 * sizeof(int)));
 
-template <int MODE>
-cudaError_t launch_pair_mode(const CUtensorMap &a, const CUtensorMap &b0, const CUtensorMap &b1, TcParams p,
-                             int max_pairs, int tail_split, int *sched_counter, void *workspace,
-                             size_t workspace_bytes, cudaStream_t stream, const YStoreMaps &ym) {
-  auto kern = tc2_kernel<MODE>;
-  const int clusters = resident_pairs<MODE>();
-  if (clusters < 1) return cudaErrorInvalidValue;
-  cudaLaunchConfig_t cfg = {};
-  cudaLaunchAttribute attr[2];
-  attr[0].id = cudaLaunchAttributeClusterDimension;
-  attr[0].val.clusterDim.x = 2;
-  attr[0].val.clusterDim.y = 1;
-  attr[0].val.clusterDim.z = 1;
-  // CTAs may start and set up while the previous kernel finishes; the kernel
-  // waits for it before its first memory access (pdl_wait).
-  attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-  attr[1].val.programmaticStreamSerializationAllowed = 1;
-  cfg.blockDim = dim3(kThreads);
-  cfg.dynamicSmemBytes = tc2_smem_bytes();
-  cfg.stream = stream;
-  cfg.attrs = attr;
-  cfg.numAttrs = 2;
-  cudaError_t e = cudaSuccess;
-  int pairs = clusters;
-  if (max_pairs >= 1 && pairs > max_pairs) pairs = max_pairs;
+// The pair kernel's work split for `pairs` resident CTA pairs (host): fills
+// p's tile order, whole-tile waves, tail split / K split and item count;
+// returns the number of pairs to launch.  Needs p.m_tiles, n_tiles,
+// num_tiles and k_blocks.  sched_counter: the dynamic schedule's counter
+// (nullptr = static); the K split needs the static schedule and room for
+// its partial sums in the workspace.
+int plan_pair_schedule(TcParams &p, int pairs, int tail_split, int *sched_counter, void *workspace,
+                       size_t workspace_bytes) {
   // Whole-tile waves, then the leftover tiles cut into g column parts.  A
   // part of width 256/g does not take 1/g of a tile: its k-blocks keep a
   // cost that does not shrink with the MMA's N (it still loads the tile's
   // whole X block; measured on B200: a quarter part takes ~0.63 of a whole
   // tile), so a part is charged (1 + 1/g) / 2 tile-times.  The last wave
   // then takes ceil(left * g / pairs) * (1 + 1/g) / 2; pick the g that
-  // makes it shortest (ties: the wider tiles).  Cutting along K instead
-  // (partial sums through L2, ordered fix-up by the last part) was built
-  // and measured slower on every shape tried (8-GPU config-3 shard: 93 us
-  // against 50 us): re-reading 128 KB of f32 rows per part costs more than
-  // the shorter wave saves.
+  // makes it shortest (ties: the wider tiles).
   //
   // Or, with the static schedule and room in the workspace, the leftover
   // tiles are cut along K into s = pairs / left parts (at most 8), one per
@@ -871,6 +851,35 @@ cudaError_t launch_pair_mode(const CUtensorMap &a, const CUtensorMap &b0, const 
   p.n_items = p.dp_waves * pairs + left * parts;
   p.dynamic = sched_counter != nullptr ? 1 : 0;
   p.sched_counter = sched_counter;
+  return pairs;
+}
+
+template <int MODE>
+cudaError_t launch_pair_mode(const CUtensorMap &a, const CUtensorMap &b0, const CUtensorMap &b1, TcParams p,
+                             int max_pairs, int tail_split, int *sched_counter, void *workspace,
+                             size_t workspace_bytes, cudaStream_t stream, const YStoreMaps &ym) {
+  auto kern = tc2_kernel<MODE>;
+  const int clusters = resident_pairs<MODE>();
+  if (clusters < 1) return cudaErrorInvalidValue;
+  cudaLaunchConfig_t cfg = {};
+  cudaLaunchAttribute attr[2];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 2;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  // CTAs may start and set up while the previous kernel finishes; the kernel
+  // waits for it before its first memory access (pdl_wait).
+  attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[1].val.programmaticStreamSerializationAllowed = 1;
+  cfg.blockDim = dim3(kThreads);
+  cfg.dynamicSmemBytes = tc2_smem_bytes();
+  cfg.stream = stream;
+  cfg.attrs = attr;
+  cfg.numAttrs = 2;
+  cudaError_t e = cudaSuccess;
+  int pairs = clusters;
+  if (max_pairs >= 1 && pairs > max_pairs) pairs = max_pairs;
+  pairs = plan_pair_schedule(p, pairs, tail_split, sched_counter, workspace, workspace_bytes);
   cfg.gridDim = dim3(2 * pairs);
   e = cudaLaunchKernelEx(&cfg, kern, a, b0, b1, p, ym);
   if (e != cudaSuccess) return e;
@@ -885,6 +894,49 @@ static_assert(kStages * kStageBytes + kStagingBytes + sizeof(PairTail) + 1024 <=
 
 size_t tc2_tail_workspace_bytes(int sm_count) {
   return kWsPartials + static_cast<size_t>(sm_count / 2) * 2 * kTailBlockBytes;
+}
+
+int tc2_schedule_items(int swiglu, int64_t M, int64_t N, int64_t K, int pairs, int tail_split, int dynamic,
+                       size_t workspace_bytes, int *items, int max_items, int *n_items, int *n_pairs, int *ksplit,
+                       int *tail_split_out) {
+  if (M < 1 || N < 1 || K < 1 || pairs < 1 || M > INT32_MAX || N > INT32_MAX || K > INT32_MAX) return -1;
+  const int tile_n = swiglu ? 128 : 256;
+  TcParams p;
+  std::memset(&p, 0, sizeof(p));
+  p.M = static_cast<int>(M);
+  p.N = static_cast<int>(N);
+  p.K = static_cast<int>(K);
+  p.m_tiles = static_cast<int>((M + 255) / 256);
+  p.n_tiles = static_cast<int>((N + tile_n - 1) / tile_n);
+  p.num_tiles = p.m_tiles * p.n_tiles;
+  p.k_blocks = static_cast<int>((K + 63) / 64);
+  // Stand-in addresses: the planner only offsets them, nothing is accessed.
+  static int counter_stand_in;
+  static char workspace_stand_in;
+  const int used = plan_pair_schedule(p, pairs, tail_split, dynamic ? &counter_stand_in : nullptr,
+                                      &workspace_stand_in, workspace_bytes);
+  *n_items = p.n_items;
+  *n_pairs = used;
+  *ksplit = p.ksplit;
+  *tail_split_out = p.tail_split;
+  for (int i = 0; i < p.n_items && i < max_items; ++i) {
+    Work w;
+    const bool ok = swiglu ? item_to_work<128>(p, used, i, w) : item_to_work<256>(p, used, i, w);
+    int mt = -1, nt = -1;
+    if (ok) tile_coords(p, w.tile, mt, nt);
+    int *o = items + 9 * static_cast<size_t>(i);
+    // static schedule: pair q takes items q, q + pairs, ...; dynamic: drawn
+    o[0] = dynamic ? -1 : i % used;
+    o[1] = ok ? mt : -1;
+    o[2] = nt;
+    o[3] = w.c0;
+    o[4] = w.wn;
+    o[5] = w.kb0;
+    o[6] = w.kb1;
+    o[7] = w.part;
+    o[8] = w.nparts;
+  }
+  return 0;
 }
 
 cudaError_t tc2_launch(int mode, const CUtensorMap &a, const CUtensorMap &b0, const CUtensorMap &b1, TcParams p,

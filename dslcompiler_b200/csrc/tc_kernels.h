@@ -95,6 +95,13 @@ constexpr size_t kTc2SchedBytes = 256;
 // Workspace the K-split tail may need on a GPU with `sm_count` SMs: the
 // counter regions and the partial sums of at most one part per pair.
 size_t tc2_tail_workspace_bytes(int sm_count);
+// The CTA-pair kernel's schedule enumerated on the host (the planner and the
+// item mapping the kernel runs): per work item 9 ints {pair (-1: dynamic),
+// row tile, column tile, first column, width, first k-block, end k-block,
+// K part, K parts}.  Returns 0, or -1 on bad arguments.
+int tc2_schedule_items(int swiglu, int64_t M, int64_t N, int64_t K, int pairs, int tail_split, int dynamic,
+                       size_t workspace_bytes, int *items, int max_items, int *n_items, int *n_pairs, int *ksplit,
+                       int *tail_split_out);
 int tc_threads();
 int tc_tile_n(int mode);
 cudaError_t tc_launch(int mode, const CUtensorMap &a, const CUtensorMap &b0, const CUtensorMap &b1,

@@ -200,6 +200,19 @@ int llk_diag_timeout_probe(int device, int64_t limit_ns);
  * shows the epilogue equals the division.  No counterpart in the reference. */
 int llk_diag_reciprocal_check(int device, uint32_t lo_bits, uint32_t hi_bits, uint64_t *mismatches);
 
+/* Diagnostic (host only, no GPU needed): the CTA-pair kernel's work split
+ * for a problem (swiglu != 0: fused SwiGLU, 128 Y columns per pair tile;
+ * else matmul, 256) on `pairs` CTA pairs, as the launch computes it --
+ * whole-tile waves, then the leftover tiles cut along N (tail_split 1, 2, 4)
+ * or along K (-s: s parts; 0 = the launch's own choice).  Writes up to
+ * max_items items of 9 int32 each: {pair (-1 when dynamic), row tile, column
+ * tile, first column, width, first k-block, end k-block, K part, K parts},
+ * and the item count, the pairs launched, the K split (0 = none) and the
+ * column split chosen.  No counterpart in the reference. */
+int llk_diag_pair_schedule(int swiglu, int64_t M, int64_t N, int64_t K, int pairs, int tail_split, int dynamic,
+                           int32_t *items, int max_items, int *n_items, int *n_pairs, int *ksplit,
+                           int *tail_split_out);
+
 /* ---- decode without device allocation -------------------------------- */
 
 /* Size of the fixed device scratch array behind llk_swiglu_decode_noalloc
