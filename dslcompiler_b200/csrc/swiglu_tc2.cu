@@ -792,13 +792,12 @@ constexpr size_t kTailBlockBytes = 128 * 256 * sizeof(float);
 constexpr int kMaxTailTiles = static_cast<int>((kWsTc2CounterBytes - kWsTc2TailCounters) / (2 * 4 * 2 * sizeof(int)));
 
 // The pair kernel's work split for `pairs` resident CTA pairs (host): fills
-// p's tile order, whole-tile waves, tail split / K split and item count;
-// returns the number of pairs to launch.  Needs p.m_tiles, n_tiles,
-// num_tiles and k_blocks.  sched_counter: the dynamic schedule's counter
-// (nullptr = static); the K split needs the static schedule and room for
-// its partial sums in the workspace.
-int plan_pair_schedule(TcParams &p, int pairs, int tail_split, int *sched_counter, void *workspace,
-                       size_t workspace_bytes) {
+// p's tile order, whole-tile waves, tail split / K split, item count and
+// dynamic flag; returns the number of pairs to launch.  Needs p.m_tiles,
+// n_tiles, num_tiles and k_blocks.  The K split needs the static schedule
+// and room for its partial sums in the workspace (workspace_bytes, 0 = no
+// workspace); the caller points p.tail_ws / tail_cnt / sched_counter at it.
+int plan_pair_schedule(TcParams &p, int pairs, int tail_split, bool dynamic, size_t workspace_bytes) {
   // Whole-tile waves, then the leftover tiles cut into g column parts.  A
   // part of width 256/g does not take 1/g of a tile: its k-blocks keep a
   // cost that does not shrink with the MMA's N (it still loads the tile's
@@ -817,8 +816,7 @@ int plan_pair_schedule(TcParams &p, int pairs, int tail_split, int *sched_counte
   const int left = p.num_tiles - p.dp_waves * pairs;
   auto ksplit_fits = [&](int ks) {
     return ks >= 2 && ks <= 8 && ks <= p.k_blocks && left > 0 && left * ks <= pairs && left <= kMaxTailTiles &&
-           sched_counter == nullptr && workspace != nullptr &&
-           workspace_bytes >= kWsPartials + static_cast<size_t>(left) * ks * 2 * kTailBlockBytes;
+           !dynamic && workspace_bytes >= kWsPartials + static_cast<size_t>(left) * ks * 2 * kTailBlockBytes;
   };
   int g = 1, ks = 0;
   if (tail_split < 0 && ksplit_fits(-tail_split)) {
@@ -842,15 +840,10 @@ int plan_pair_schedule(TcParams &p, int pairs, int tail_split, int *sched_counte
   p.ksplit = ks;
   p.tail_split = ks ? 1 : g;
   const int parts = ks ? ks : g;
-  if (ks) {
-    p.tail_ws = reinterpret_cast<float *>(static_cast<char *>(workspace) + kWsPartials);
-    p.tail_cnt = reinterpret_cast<int *>(static_cast<char *>(workspace) + kWsTc2TailCounters);
-  }
   // No pair without work: at most all tiles' parts.
   if (p.dp_waves == 0 && pairs > left * parts) pairs = left * parts;
   p.n_items = p.dp_waves * pairs + left * parts;
-  p.dynamic = sched_counter != nullptr ? 1 : 0;
-  p.sched_counter = sched_counter;
+  p.dynamic = dynamic ? 1 : 0;
   return pairs;
 }
 
@@ -879,7 +872,12 @@ cudaError_t launch_pair_mode(const CUtensorMap &a, const CUtensorMap &b0, const 
   cudaError_t e = cudaSuccess;
   int pairs = clusters;
   if (max_pairs >= 1 && pairs > max_pairs) pairs = max_pairs;
-  pairs = plan_pair_schedule(p, pairs, tail_split, sched_counter, workspace, workspace_bytes);
+  pairs = plan_pair_schedule(p, pairs, tail_split, sched_counter != nullptr, workspace ? workspace_bytes : 0);
+  if (p.ksplit) {
+    p.tail_ws = reinterpret_cast<float *>(static_cast<char *>(workspace) + kWsPartials);
+    p.tail_cnt = reinterpret_cast<int *>(static_cast<char *>(workspace) + kWsTc2TailCounters);
+  }
+  p.sched_counter = sched_counter;
   cfg.gridDim = dim3(2 * pairs);
   e = cudaLaunchKernelEx(&cfg, kern, a, b0, b1, p, ym);
   if (e != cudaSuccess) return e;
@@ -910,11 +908,7 @@ int tc2_schedule_items(int swiglu, int64_t M, int64_t N, int64_t K, int pairs, i
   p.n_tiles = static_cast<int>((N + tile_n - 1) / tile_n);
   p.num_tiles = p.m_tiles * p.n_tiles;
   p.k_blocks = static_cast<int>((K + 63) / 64);
-  // Stand-in addresses: the planner only offsets them, nothing is accessed.
-  static int counter_stand_in;
-  static char workspace_stand_in;
-  const int used = plan_pair_schedule(p, pairs, tail_split, dynamic ? &counter_stand_in : nullptr,
-                                      &workspace_stand_in, workspace_bytes);
+  const int used = plan_pair_schedule(p, pairs, tail_split, dynamic != 0, workspace_bytes);
   *n_items = p.n_items;
   *n_pairs = used;
   *ksplit = p.ksplit;
